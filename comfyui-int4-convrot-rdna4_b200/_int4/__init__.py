@@ -1,0 +1,118 @@
+"""ConvRot W4A4 forward path for NVIDIA B200 (sm_100a).
+
+Drop-in replacement for the ``_int4`` package of ComfyUI-INT4-ConvRot-RDNA4
+(reference API: _int4/__init__.py:9-14, :35-42). The node code calls
+
+    quantize_convrot_w4a4_weight(weight, convrot_groupsize) -> (qweight_i8, scale_f32)
+    convrot_w4a4_linear(x, qweight, wscales, bias, convrot_groupsize) -> tensor
+    is_available() -> bool          # sm_100 device + loadable CUDA library
+    pick_groupsize(in_features) -> int | None
+
+with the same signatures, packed-weight layout and errors. Every int4 forward
+runs two CUDA kernels from libconvrot_b200.so (fused rotate+quantize, then the
+tcgen05 GEMM with the dequant/bias epilogue); there is no torch or CPU
+fallback, so a missing library raises.
+"""
+from __future__ import annotations
+
+import torch
+
+from ._codec import _INT4_GROUP_SIZE
+from .cuda_loader import convrot_quant_int4, int4_convrot_gemm
+from .cuda_loader import is_available as _lib_available
+from .eager import (
+    _build_hadamard,
+    _rotate_activation,
+    dequantize_convrot_w4a4_weight,
+    quantize_convrot_w4a4_weight,
+    quantize_signed_int4_rowwise,
+)
+from .int8_eager import convrot_w8a8_linear as _torch_convrot_w8a8_linear
+
+__all__ = [
+    "quantize_convrot_w4a4_weight",
+    "dequantize_convrot_w4a4_weight",
+    "convrot_w4a4_linear",
+    "convrot_w8a8_linear",
+    "is_available",
+    "pick_groupsize",
+]
+
+# Output dtypes the GEMM epilogue writes directly; others compute f32 then cast.
+_NATIVE_OUT = frozenset({torch.float32, torch.bfloat16})
+
+
+def pick_groupsize(in_features: int) -> int | None:
+    """Largest supported ConvRot group size (256, 64, 16) dividing in_features."""
+    for g in (256, 64, 16):
+        if in_features % g == 0:
+            return g
+    return None
+
+
+def _is_sm100() -> bool:
+    if not torch.cuda.is_available():
+        return False
+    try:
+        major, _minor = torch.cuda.get_device_capability(0)
+    except Exception:
+        return False
+    return major == 10
+
+
+def is_available() -> bool:
+    """True only on an sm_100 (B200-class) CUDA device with a loadable library."""
+    return _is_sm100() and _lib_available()
+
+
+def _validate(x, qweight, convrot_groupsize, quant_group_size, linear_dtype) -> None:
+    if linear_dtype not in ("int4", "int8"):
+        raise ValueError(f"ConvRot W4A4 linear_dtype must be 'int4' or 'int8', got {linear_dtype!r}")
+    if quant_group_size != _INT4_GROUP_SIZE:
+        raise ValueError(f"int4 MMA kernel requires quant_group_size {_INT4_GROUP_SIZE}")
+    if x.shape[-1] != qweight.shape[-1] * 2:
+        raise ValueError(f"Input K={x.shape[-1]} does not match qweight K={qweight.shape[-1] * 2}")
+    if x.shape[-1] % convrot_groupsize != 0:
+        raise ValueError(f"Input K={x.shape[-1]} not divisible by convrot_groupsize {convrot_groupsize}")
+
+
+def convrot_w4a4_linear(
+    x: torch.Tensor,
+    qweight: torch.Tensor,
+    wscales: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    convrot_groupsize: int = 256,
+    quant_group_size: int = _INT4_GROUP_SIZE,
+    linear_dtype: str = "int4",
+) -> torch.Tensor:
+    """``x @ W.T + bias`` through the B200 int4 ConvRot kernels.
+
+    x [..., K] (bf16, fp16 or fp32, CUDA), qweight int8 [N, K/2] packed,
+    wscales [N], bias [N] or None. Returns [..., N] in x.dtype.
+    ``linear_dtype='int8'`` is accepted like the reference, whose eager path
+    computes the same int4 product for it (_int4/eager.py:172-197).
+    """
+    _validate(x, qweight, convrot_groupsize, quant_group_size, linear_dtype)
+    shape = x.shape
+    x2d = x.reshape(-1, shape[-1]).contiguous()
+    qact, x_scale = convrot_quant_int4(x2d, convrot_groupsize)
+    out_dtype = x.dtype if x.dtype in _NATIVE_OUT else torch.float32
+    out = int4_convrot_gemm(qact, qweight, x_scale, wscales, bias, out_dtype)
+    if out.dtype != x.dtype:
+        out = out.to(x.dtype)
+    return out.reshape(*shape[:-1], qweight.shape[0])
+
+
+def convrot_w8a8_linear(
+    x: torch.Tensor,
+    qweight: torch.Tensor,
+    wscales: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    convrot_groupsize: int = 256,
+) -> torch.Tensor:
+    """``x @ W.T + bias`` for int8 ConvRot layers (qweight int8 [N, K], wscales [N]).
+
+    Computed with torch ops on the input's device (the int8 tier has no sm_100a
+    kernel yet).
+    """
+    return _torch_convrot_w8a8_linear(x, qweight, wscales, bias=bias, convrot_groupsize=convrot_groupsize)

@@ -1,0 +1,184 @@
+"""ctypes binding of libconvrot_b200.so (the sm_100a kernels).
+
+Counterpart of the reference's hip_loader.py (_int4/hip_loader.py:42-207):
+same Python functions, same argument meaning, outputs allocated by torch on
+the input's device, calls issued on torch's current stream, RuntimeError on a
+nonzero return code. There is no fallback: if the library cannot be loaded
+every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import build as _build
+
+_lib = None
+_lock = threading.Lock()
+
+_OUT_DTYPE_CODE = {torch.float32: 0, torch.bfloat16: 1}
+_IN_DTYPE_CODE = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_SIGNATURES = {
+    "ck_convrot_quant_int4": [_P, _I, _P, _P, _I, _I, _I, _P],
+    "ck_int4_quant_rowwise": [_P, _I, _P, _P, _I, _I, _P],
+    "ck_int4_convrot_gemm": [_P] * 6 + [_I] * 4 + [_P],
+    "ck_int4_convrot_gemm_splitk": [_P] * 5 + [_I] * 4 + [_P],
+    "ck_int4_gemm_s32": [_P, _P, _P, _I, _I, _I, _P],
+    "ck_convrot_device_status": [_P, ctypes.POINTER(ctypes.c_int)],
+    "ck_convrot_last_error": [],
+}
+
+
+def _load():
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            path = _build.lib_path()
+            if not __import__("os").path.exists(path):
+                _build.build()
+            lib = ctypes.CDLL(path)
+            for name, argtypes in _SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = argtypes
+                fn.restype = ctypes.c_char_p if name == "ck_convrot_last_error" else ctypes.c_int
+            _lib = lib
+    return _lib
+
+
+def library():
+    """The loaded ctypes library (builds it first if the .so is missing)."""
+    return _load()
+
+
+def _check(name: str, rc: int) -> None:
+    if rc == 0:
+        return
+    if rc == -1:
+        msg = _load().ck_convrot_last_error().decode(errors="replace")
+        raise RuntimeError(f"{name} rejected its arguments: {msg}")
+    raise RuntimeError(f"{name} failed, cudaError={rc}")
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError("the B200 ConvRot kernels need CUDA tensors")
+
+
+def convrot_quant_int4(x: torch.Tensor, convrot_groupsize: int):
+    """Fused rotation + row-wise int4 quantization: (packed int8 [M, K/2], scale f32 [M])."""
+    lib = _load()
+    if convrot_groupsize not in (16, 64, 256):
+        raise ValueError("fused convrot_quant_int4 supports groupsize 16/64/256")
+    _require_cuda(x)
+    if x.dtype not in _IN_DTYPE_CODE:
+        raise ValueError(f"unsupported activation dtype {x.dtype}")
+    x = x.contiguous()
+    m, k = x.shape
+    qout = torch.empty((m, k // 2), dtype=torch.int8, device=x.device)
+    scale = torch.empty((m,), dtype=torch.float32, device=x.device)
+    rc = lib.ck_convrot_quant_int4(x.data_ptr(), _IN_DTYPE_CODE[x.dtype], qout.data_ptr(),
+                                   scale.data_ptr(), m, k, convrot_groupsize, _stream(x))
+    _check("ck_convrot_quant_int4", rc)
+    return qout, scale
+
+
+def int4_quant_rowwise(x_rot: torch.Tensor):
+    """Row-wise int4 quantization of an already rotated activation."""
+    lib = _load()
+    _require_cuda(x_rot)
+    if x_rot.dtype not in _IN_DTYPE_CODE:
+        raise ValueError(f"unsupported activation dtype {x_rot.dtype}")
+    x_rot = x_rot.contiguous()
+    m, k = x_rot.shape
+    qout = torch.empty((m, k // 2), dtype=torch.int8, device=x_rot.device)
+    scale = torch.empty((m,), dtype=torch.float32, device=x_rot.device)
+    rc = lib.ck_int4_quant_rowwise(x_rot.data_ptr(), _IN_DTYPE_CODE[x_rot.dtype], qout.data_ptr(),
+                                   scale.data_ptr(), m, k, _stream(x_rot))
+    _check("ck_int4_quant_rowwise", rc)
+    return qout, scale
+
+
+def _packed_pair(x_packed: torch.Tensor, w_packed: torch.Tensor):
+    _require_cuda(x_packed, w_packed)
+    x_packed = x_packed.contiguous()
+    w_packed = w_packed.contiguous()
+    m, kp = x_packed.shape
+    n, kp2 = w_packed.shape
+    if kp != kp2:
+        raise ValueError(f"K mismatch: x {tuple(x_packed.shape)} w {tuple(w_packed.shape)}")
+    return x_packed, w_packed, m, n, kp * 2
+
+
+def int4_convrot_gemm(x_packed, w_packed, x_scale, w_scale, bias, out_dtype):
+    """out[M,N] = (Xint @ Wint^T) * x_scale[:,None] * w_scale[None,:] (+ bias)."""
+    lib = _load()
+    if out_dtype not in _OUT_DTYPE_CODE:
+        raise ValueError(f"int4 gemm output dtype must be float32/bfloat16, got {out_dtype}")
+    x_packed, w_packed, m, n, k = _packed_pair(x_packed, w_packed)
+    x_scale = x_scale.to(torch.float32).contiguous()
+    w_scale = w_scale.to(torch.float32).contiguous()
+    out = torch.empty((m, n), dtype=out_dtype, device=x_packed.device)
+    bias_ptr = 0
+    if bias is not None:
+        bias = bias.to(torch.float32).contiguous()
+        bias_ptr = bias.data_ptr()
+    rc = lib.ck_int4_convrot_gemm(x_packed.data_ptr(), w_packed.data_ptr(), x_scale.data_ptr(),
+                                  w_scale.data_ptr(), bias_ptr, out.data_ptr(), m, n, k,
+                                  _OUT_DTYPE_CODE[out_dtype], _stream(x_packed))
+    _check("ck_int4_convrot_gemm", rc)
+    return out
+
+
+def int4_convrot_gemm_splitk(x_packed, w_packed, x_scale, w_scale, accum, nsplit: int = 1):
+    """accum += (Xint @ Wint^T) * x_scale[:,None] * w_scale[None,:] (f32, in place)."""
+    lib = _load()
+    x_packed, w_packed, m, n, k = _packed_pair(x_packed, w_packed)
+    if accum.dtype != torch.float32 or tuple(accum.shape) != (m, n) or not accum.is_contiguous():
+        raise ValueError("accum must be a contiguous float32 [M, N] tensor")
+    x_scale = x_scale.to(torch.float32).contiguous()
+    w_scale = w_scale.to(torch.float32).contiguous()
+    rc = lib.ck_int4_convrot_gemm_splitk(x_packed.data_ptr(), w_packed.data_ptr(), x_scale.data_ptr(),
+                                         w_scale.data_ptr(), accum.data_ptr(), m, n, k, nsplit,
+                                         _stream(x_packed))
+    _check("ck_int4_convrot_gemm_splitk", rc)
+    return accum
+
+
+def int4_gemm_s32(x_packed, w_packed):
+    """Exact int32 accumulators [M, N] of the packed-code product."""
+    lib = _load()
+    x_packed, w_packed, m, n, k = _packed_pair(x_packed, w_packed)
+    acc = torch.empty((m, n), dtype=torch.int32, device=x_packed.device)
+    rc = lib.ck_int4_gemm_s32(x_packed.data_ptr(), w_packed.data_ptr(), acc.data_ptr(), m, n, k,
+                              _stream(x_packed))
+    _check("ck_int4_gemm_s32", rc)
+    return acc
+
+
+def device_status(device=None) -> int:
+    """Read and clear the kernels' bounded-wait status word (0 = ok)."""
+    lib = _load()
+    st = ctypes.c_int(0)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    _check("ck_convrot_device_status", lib.ck_convrot_device_status(stream, ctypes.byref(st)))
+    return st.value
+
+
+def is_available() -> bool:
+    try:
+        _load()
+        return True
+    except Exception:
+        return False

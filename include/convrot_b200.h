@@ -1,0 +1,81 @@
+/*
+ * C ABI of the B200 (sm_100a) ConvRot W4A4 library, libconvrot_b200.so.
+ *
+ * Drop-in for the HIP library of 0xDELUXA/ComfyUI-INT4-ConvRot-RDNA4
+ * (_int4/int4_gemm.hip). Paths below are relative to that project.
+ *
+ * Conventions (same as the reference exports, _int4/int4_gemm.hip:627-741):
+ *   - all pointers are device pointers; the caller allocates every output;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
+ *   - launches are asynchronous and nothing synchronises inside a call;
+ *   - return 0 on success, -1 when a shape/pointer precondition fails (nothing
+ *     is launched; ck_convrot_last_error() explains), otherwise a cudaError_t.
+ *
+ * Layouts (the reference codec, _int4/_codec.py:19-36):
+ *   packed int4 matrix [rows, K/2] int8, row-major; byte j of a row holds
+ *   column 2j in its low nibble and column 2j+1 in its high nibble, both two's
+ *   complement. Scales are float32, one per row (tokens) / output channel.
+ */
+#ifndef CONVROT_B200_H
+#define CONVROT_B200_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Fused ConvRot rotation + row-wise int4 quantization + packing.
+ * Replaces ck_convrot_quant_int4 (_int4/int4_gemm.hip:650-660), bound by
+ * convrot_quant_int4 (_int4/hip_loader.py:74-92).
+ *   x        [M, K] activations, in_dtype 0 = f32, 1 = bf16, 2 = f16
+ *   qout     [M, K/2] int8 packed codes
+ *   scaleout [M] f32 row scales
+ * G in {16, 64, 256}, K % G == 0, K % 16 == 0. Quantizer arithmetic follows
+ * the eager path (_int4/eager.py:112-120) in the activation dtype. */
+int ck_convrot_quant_int4(const void* x, int in_dtype, void* qout, void* scaleout,
+                          int M, int K, int G, void* stream);
+
+/* Row-wise int4 quantization + packing of an already rotated activation
+ * (rotation skipped). Replaces quantize_signed_int4_rowwise
+ * (_int4/eager.py:112-120) for device tensors; same arguments as above minus G. */
+int ck_int4_quant_rowwise(const void* x, int in_dtype, void* qout, void* scaleout,
+                          int M, int K, void* stream);
+
+/* out[m, n] = ((float(D[m, n]) * xscale[m]) * wscale[n]) + bias[n],
+ * D = exact int32 sum_k X[m, k] * W[n, k] over packed codes.
+ * Replaces ck_int4_convrot_gemm (_int4/int4_gemm.hip:711-741), bound by
+ * int4_convrot_gemm (_int4/hip_loader.py:158-207).
+ *   Xp [M, K/2], Wp [N, K/2] packed int8 (16-byte aligned)
+ *   xscale [M], wscale [N], bias [N] or NULL: f32
+ *   out [M, N], out_dtype 0 = f32, 1 = bf16
+ * K % 32 == 0 and K <= 65536. */
+int ck_int4_convrot_gemm(const void* Xp, const void* Wp, const void* xscale, const void* wscale,
+                         const void* bias, void* out, int M, int N, int K, int out_dtype,
+                         void* stream);
+
+/* accum[m, n] += (float(D[m, n]) * xscale[m]) * wscale[n] into a caller-zeroed
+ * f32 [M, N] buffer. Replaces ck_int4_convrot_gemm_splitk
+ * (_int4/int4_gemm.hip:634-645). The reference splits K and adds float
+ * partials with atomics; here D is reduced in int32 first, so the result is
+ * deterministic. `nsplit` (>= 1) is accepted for ABI compatibility. */
+int ck_int4_convrot_gemm_splitk(const void* Xp, const void* Wp, const void* xscale,
+                                const void* wscale, void* accum, int M, int N, int K,
+                                int nsplit, void* stream);
+
+/* Raw exact int32 accumulators acc[M, N] = sum_k X[m, k] * W[n, k].
+ * No reference counterpart as an export: the reference computes these inside
+ * its GEMM (_int4/int4_gemm.hip:204-232); exposed for bit-exact parity checks. */
+int ck_int4_gemm_s32(const void* Xp, const void* Wp, void* acc, int M, int N, int K, void* stream);
+
+/* Reads and clears the device status word that kernels set when a bounded
+ * wait gives up (0 = ok). Synchronises `stream`. No reference counterpart:
+ * the reference has no device-side timeouts. */
+int ck_convrot_device_status(void* stream, int* status);
+
+/* Human-readable reason for the last -1 returned on this host thread. */
+const char* ck_convrot_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CONVROT_B200_H */

@@ -1,0 +1,110 @@
+"""C-ABI and host-logic checks that need no GPU.
+
+The library must load and export every function declared in
+include/convrot_b200.h; precondition failures return -1 before any CUDA call
+(the reference's convention, _int4/int4_gemm.hip:637, :653, :715).
+"""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+import _int4
+from _int4 import build as libbuild
+from _int4 import cuda_loader
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "convrot_b200.h")
+
+
+def header_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return re.findall(r"\b(?:int|const char\*)\s+(ck_\w+)\s*\(", text)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(libbuild.lib_path()):
+        libbuild.build()
+    return cuda_loader.library()
+
+
+def test_header_symbols_exported(lib):
+    names = header_functions()
+    assert len(names) >= 7
+    raw = ctypes.CDLL(libbuild.lib_path())
+    for n in names:
+        assert hasattr(raw, n), n
+
+
+def test_only_header_symbols_are_public(lib):
+    """-fvisibility=hidden: nothing but the ck_* API leaks from the library."""
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", libbuild.lib_path()], capture_output=True, text=True)
+    if out.returncode != 0:
+        pytest.skip("nm unavailable")
+    ck = {line.split()[-1] for line in out.stdout.splitlines() if " T ck_" in line}
+    assert ck == set(header_functions())
+
+
+@pytest.mark.parametrize("k", [0, 48, 65568])
+def test_gemm_rejects_bad_k(lib, k):
+    rc = lib.ck_int4_convrot_gemm(16, 16, 16, 16, 0, 16, 4, 4, k, 1, None)
+    assert rc == -1
+    assert b"K" in lib.ck_convrot_last_error()
+
+
+def test_gemm_rejects_bad_out_dtype_and_alignment(lib):
+    assert lib.ck_int4_convrot_gemm(16, 16, 16, 16, 0, 16, 4, 4, 64, 7, None) == -1
+    assert lib.ck_int4_convrot_gemm(17, 16, 16, 16, 0, 16, 4, 4, 64, 1, None) == -1
+    assert b"aligned" in lib.ck_convrot_last_error()
+    assert lib.ck_int4_convrot_gemm(0, 0, 16, 16, 0, 16, 4, 4, 64, 1, None) == -1
+
+
+def test_gemm_empty_is_noop(lib):
+    assert lib.ck_int4_convrot_gemm(16, 16, 16, 16, 0, 16, 0, 4, 64, 1, None) == 0
+    assert lib.ck_int4_gemm_s32(16, 16, 16, 4, 0, 64, None) == 0
+
+
+def test_splitk_rejects_bad_nsplit(lib):
+    assert lib.ck_int4_convrot_gemm_splitk(16, 16, 16, 16, 16, 4, 4, 64, 0, None) == -1
+
+
+@pytest.mark.parametrize("g,k", [(32, 512), (256, 320), (64, 96)])
+def test_quant_rejects_bad_group(lib, g, k):
+    assert lib.ck_convrot_quant_int4(16, 1, 16, 16, 4, k, g, None) == -1
+
+
+def test_quant_rejects_bad_dtype_and_k(lib):
+    assert lib.ck_convrot_quant_int4(16, 3, 16, 16, 4, 256, 256, None) == -1
+    assert lib.ck_int4_quant_rowwise(16, 1, 16, 16, 4, 24, None) == -1
+    assert lib.ck_convrot_quant_int4(16, 1, 16, 16, 0, 256, 256, None) == 0
+
+
+def test_python_api_validation_errors():
+    x = torch.zeros(4, 512, dtype=torch.bfloat16)
+    qw = torch.zeros(8, 256, dtype=torch.int8)
+    ws = torch.ones(8)
+    with pytest.raises(ValueError, match="linear_dtype"):
+        _int4.convrot_w4a4_linear(x, qw, ws, linear_dtype="fp8")
+    with pytest.raises(ValueError, match="quant_group_size"):
+        _int4.convrot_w4a4_linear(x, qw, ws, quant_group_size=32)
+    with pytest.raises(ValueError, match="does not match"):
+        _int4.convrot_w4a4_linear(x, qw[:, :128], ws)
+    with pytest.raises(ValueError, match="divisible"):
+        _int4.convrot_w4a4_linear(torch.zeros(4, 320, dtype=torch.bfloat16), qw[:, :160], ws, convrot_groupsize=256)
+    with pytest.raises(ValueError, match="CUDA"):
+        _int4.convrot_w4a4_linear(x, qw, ws)
+
+
+def test_pick_groupsize_and_availability():
+    assert _int4.pick_groupsize(3072) == 256
+    assert _int4.pick_groupsize(15360) == 256
+    assert _int4.pick_groupsize(320) == 64
+    assert _int4.pick_groupsize(48) == 16
+    assert _int4.pick_groupsize(40) is None
+    if not torch.cuda.is_available():
+        assert _int4.is_available() is False
