@@ -1,0 +1,456 @@
+"""Benchmark of the B200 ConvRot W4A4 linear path.
+
+One step = the Flux-class double-block linear set at M = 4608 tokens:
+QKV 3072->9216, attention-out 3072->3072, MLP-up 3072->12288 and MLP-down
+12288->3072, each a full W4A4 forward (fused rotate+quantize kernel, then the
+tcgen05 int4 GEMM with the dequant + bias epilogue). Metric: W4A4 linear TOPS
+(2*M*N*K ops per layer; integer MACs count as two ops).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one process per GPU: token-parallel replicas (each
+rank runs its own 4608-token step with replicated weights, no collective on
+the data path), weak scaling; the step time is the max over ranks.
+
+``--impl reference`` times the CPU restatement of the reference algorithm
+(oracle/convrot_oracle.py, the port of _int4/eager.py + the HIP epilogue) on
+the host cores, rank 0 only.
+
+Timing: inputs are resident in HBM; L2 is flushed (a 256 MiB write) before
+every timed step; each step is bracketed by CUDA events on the launching
+stream and the K durations are summed.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "comfyui-int4-convrot-rdna4_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+M_TOKENS = 4608
+HIDDEN = 3072
+LAYERS = [("qkv", 3072, 9216), ("attn_out", 3072, 3072), ("mlp_up", 3072, 12288), ("mlp_down", 12288, 3072)]
+GROUP = 256
+METRIC = "w4a4_linear_tops"
+UNIT = "TOPS"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def step_ops(m: int) -> int:
+    return sum(2 * m * n * k for _, k, n in LAYERS)
+
+
+def workload_config(extra=None):
+    cfg = {"workload": "config1_flux_double_block_linears", "tokens_per_gpu": M_TOKENS, "hidden": HIDDEN,
+           "layers": {name: f"{k}->{n}" for name, k, n in LAYERS}, "convrot_groupsize": GROUP,
+           "l2": "flushed before every timed step (256 MiB write)"}
+    if extra:
+        cfg.update(extra)
+    return cfg
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        return json.load(f)
+
+
+def synth_activation(m, k, gen, device):
+    x = torch.randn(m, k, generator=gen)
+    idx = torch.randperm(k, generator=gen)[: max(1, k // 100)]
+    x[:, idx] *= 20.0
+    return x.to(torch.bfloat16).to(device)
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._drain, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _drain(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[4:8]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- CPU arm
+
+class CpuWorkload:
+    """The oracle port of the reference path (all four layers) on `rows` tokens."""
+
+    def __init__(self, rows: int, seed: int = 0):
+        from oracle import convrot_oracle as orc
+        self.orc = orc
+        self.rows = rows
+        rng = np.random.default_rng(seed)
+        self.layers = []
+        for _, k, n in LAYERS:
+            w = (rng.standard_normal((n, k), dtype=np.float32) * 0.02).astype(np.float16)
+            wp, ws = orc.quantize_weight(w, GROUP, "f16")
+            bias = (rng.standard_normal(n, dtype=np.float32) * 0.01).astype(np.float16).astype(np.float32)
+            x = rng.standard_normal((rows, k), dtype=np.float32)
+            x[:, rng.permutation(k)[: k // 100]] *= 20
+            # weights stay decoded across steps, like resident device weights
+            self.layers.append((orc.f32_to_bf16_bits(x), orc.decode_weight(wp), ws, bias))
+
+    def step(self) -> float:
+        t0 = time.perf_counter()
+        for x, wcodes, ws, bias in self.layers:
+            self.orc.convrot_w4a4_linear_decoded(x, wcodes, ws, bias, GROUP)
+        return time.perf_counter() - t0
+
+
+def cpu_sample(rows: int, budget_s: float, seed: int = 0):
+    """Median step time of the oracle port over about `budget_s` seconds: (TOPS, s, steps)."""
+    wl = CpuWorkload(rows, seed)
+    wl.step()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < 2 or time.perf_counter() < t_end:
+        times.append(wl.step())
+    t = statistics.median(times)
+    return step_ops(rows) / t / 1e12, t, len(times)
+
+
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads") for i in threadpool_info() if i.get("user_api") == "blas"]
+        if n:
+            return int(max(n))
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    rows = args.cpu_rows
+    wl = CpuWorkload(rows)
+    for _ in range(args.warmup):
+        wl.step()
+    times = [wl.step() for _ in range(args.steps)]
+    t = statistics.median(times)
+    value = step_ops(rows) / t / 1e12
+    sample = f"{rows} of {M_TOKENS} tokens per step through all four layers (oracle port, numpy + BLAS)"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3 * M_TOKENS / rows,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4",
+        "data": "synthetic (seeded; config-1 shapes and value distributions)",
+        "config": workload_config({"cpu_rows_per_step": rows}),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU arm
+
+def build_layers(device, seed):
+    import _int4
+    gen = torch.Generator().manual_seed(seed)
+    layers = []
+    for name, k, n in LAYERS:
+        w = (torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16).to(device)
+        qw, ws = _int4.quantize_convrot_w4a4_weight(w.to(torch.float16), GROUP)
+        bias = (torch.randn(n, generator=gen) * 0.01).to(torch.bfloat16).to(torch.float16).to(device)
+        layers.append({"name": name, "k": k, "n": n, "qw": qw, "ws": ws, "bias": bias,
+                       "bias32": bias.float().contiguous()})
+        del w
+    xs = {k: synth_activation(M_TOKENS, k, gen, device) for k in sorted({k for _, k, _ in LAYERS})}
+    return layers, xs
+
+
+def device_step(layers, xs):
+    """One config-1 step through the public API on device-resident inputs."""
+    import _int4
+    return [_int4.convrot_w4a4_linear(xs[l["k"]], l["qw"], l["ws"], l["bias"], GROUP) for l in layers]
+
+
+def time_kernel(fn, iters, flush, stream):
+    """Average device time (ms) of fn() over `iters`, L2 flushed before each."""
+    total = 0.0
+    for _ in range(iters):
+        flush()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        b.synchronize()
+        total += a.elapsed_time(b)
+    return total / iters
+
+
+def run_ours(args, rank, world, local_rank):
+    import _int4
+    from _int4 import cuda_loader as ck
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    assert _int4.is_available(), "libconvrot_b200.so must load on an sm_100 device"
+    stream = torch.cuda.current_stream(device)
+    flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+
+    def flush():
+        flush_buf.fill_(1.0)
+
+    layers, xs = build_layers(device, seed=1234 + rank)
+    for _ in range(args.warmup):
+        flush()
+        device_step(layers, xs)
+    torch.cuda.synchronize()
+
+    # ---------------- timed region: K steps, barrier + sync on both sides
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    events = []
+    for _ in range(args.steps):
+        flush()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        device_step(layers, xs)
+        b.record(stream)
+        events.append((a, b))
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    clocks = sampler.stop()
+    elapsed_ms = sum(a.elapsed_time(b) for a, b in events)
+    if world > 1:
+        t = torch.tensor([elapsed_ms], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    ms_per_step = elapsed_ms / args.steps
+    value = world * step_ops(M_TOKENS) / (ms_per_step * 1e-3) / 1e12
+
+    # ---------------- per-kernel roofline (dominant GEMM = MLP up), rank 0
+    extras = {}
+    if rank == 0:
+        peaks, peak_src = load_peaks()
+        up = next(l for l in layers if l["name"] == "mlp_up")
+        xq, xsc = ck.convrot_quant_int4(xs[up["k"]], GROUP)
+        iters = 10
+        gemm_ms = time_kernel(lambda: ck.int4_convrot_gemm(xq, up["qw"], xsc, up["ws"], up["bias32"],
+                                                           torch.bfloat16), iters, flush, stream)
+        quant_ms = time_kernel(lambda: ck.convrot_quant_int4(xs[up["k"]], GROUP), iters, flush, stream)
+        m, k, n = M_TOKENS, up["k"], up["n"]
+        gemm_ops = 2 * m * n * k
+        int8_peak = 2.0 * peaks["bf16_tflops"]           # dense int8 rate = 2x bf16 on B200
+        achieved = gemm_ops / (gemm_ms * 1e-3) / 1e12
+        traffic = load_traffic()
+        extras["roofline"] = {
+            "kernel": "int4_gemm_kernel (MLP up 3072->12288, M=4608)",
+            "bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
+            "frac": achieved / int8_peak,
+            "peak_source": f"2 x {peak_src} bf16 burst ({peaks['bf16_tflops']} TFLOP/s): B200 dense int8 rate",
+            "ms_per_launch": gemm_ms,
+            "traffic": traffic.get("int4_gemm_kernel_bytes_per_launch") if traffic else None,
+            "algorithmic_bytes": m * k // 2 + n * k // 2 + 4 * m + 4 * n + 4 * n + 2 * m * n,
+        }
+        qbytes = 2 * m * k + m * k // 2 + 4 * m
+        extras["quant_kernel"] = {
+            "kernel": "convrot_quant_kernel (K=3072, M=4608)", "bound": "hbm",
+            "achieved": qbytes / (quant_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": qbytes / (quant_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "ms_per_launch": quant_ms,
+        }
+        # small-M (weight-bound) layer: Flux modulation 3072 -> 18432 at M = 1
+        wsm = (torch.randn(18432, 3072, device=device) * 0.02).to(torch.float16)
+        qsm, wssm = _int4.quantize_convrot_w4a4_weight(wsm, GROUP)
+        del wsm
+        x1 = synth_activation(1, 3072, torch.Generator().manual_seed(5), device)
+        x1q, x1s = ck.convrot_quant_int4(x1, GROUP)
+        sm_ms = time_kernel(lambda: ck.int4_convrot_gemm(x1q, qsm, x1s, wssm, None, torch.bfloat16),
+                            iters, flush, stream)
+        sm_bytes = 3072 // 2 + 18432 * 3072 // 2 + 4 + 4 * 18432 + 2 * 18432
+        extras["small_m"] = {
+            "kernel": "int4_gemm_kernel (modulation 3072->18432, M=1)", "bound": "hbm",
+            "achieved": sm_bytes / (sm_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": sm_bytes / (sm_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "ms_per_launch": sm_ms,
+        }
+
+    # ---------------- end to end: host buffers in, host buffers out, through the public API
+    host_in = {k: v.cpu().pin_memory() for k, v in xs.items()}
+    host_out = [torch.empty((M_TOKENS, l["n"]), dtype=torch.bfloat16).pin_memory() for l in layers]
+    h2d = sum(v.numel() * v.element_size() for v in host_in.values())
+    d2h = sum(v.numel() * v.element_size() for v in host_out)
+
+    def e2e_step():
+        dev_in = {k: v.to(device, non_blocking=True) for k, v in host_in.items()}
+        outs = device_step(layers, dev_in)
+        for o, h in zip(outs, host_out):
+            h.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_steps = max(3, min(args.steps, 10))
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * step_ops(M_TOKENS) / (e2e_ms * 1e-3) / 1e12
+
+    if rank == 0:
+        cpu_tops, cpu_t, _ = cpu_sample(args.cpu_rows, args.cpu_seconds) if world == 1 else (None, None, None)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int4",
+            "data": "synthetic (seeded N(0,1) activations with 1% x20 outlier channels, N(0,0.02) weights)",
+            "config": workload_config({"parallelism": f"token-parallel replicas x{world}"}),
+            "gpu_launches": 2 * len(LAYERS) * args.steps,
+            "clocks": clocks,
+            "e2e": {"value": e2e_value, "unit": UNIT, "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            **extras,
+        }
+        if cpu_tops is not None:
+            line["cpu_baseline"] = {"value": cpu_tops, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                                    "sample": f"{args.cpu_rows} tokens through all four layers, "
+                                              f"median over ~{args.cpu_seconds:.0f} s (oracle port)"}
+        print(json.dumps(line), flush=True)
+
+
+def run_case(args):
+    """A few launches of one kernel on its own, for ncu captures (no timing, no flush)."""
+    import _int4
+    from _int4 import cuda_loader as ck
+    device = torch.device("cuda", 0)
+    gen = torch.Generator().manual_seed(0)
+    if args.case == "small_m":
+        m, k, n = 1, 3072, 18432
+    else:
+        m, k, n = M_TOKENS, 3072, 12288
+    w = (torch.randn(n, k, generator=gen) * 0.02).to(torch.float16).to(device)
+    qw, ws = _int4.quantize_convrot_w4a4_weight(w, GROUP)
+    bias = torch.zeros(n, device=device)
+    x = synth_activation(m, k, gen, device)
+    xq, xsc = ck.convrot_quant_int4(x, GROUP)
+    for _ in range(args.iters):
+        if args.case == "quant":
+            ck.convrot_quant_int4(x, GROUP)
+        else:
+            ck.int4_convrot_gemm(xq, qw, xsc, ws, bias, torch.bfloat16)
+    torch.cuda.synchronize()
+    print(json.dumps({"case": args.case, "m": m, "k": k, "n": n, "iters": args.iters}))
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-rows", type=int, default=256, help="tokens per CPU-baseline sample")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline time budget")
+    ap.add_argument("--case", choices=["mlp_up", "small_m", "quant"], default=None,
+                    help="run one kernel --iters times (profiling helper) instead of the benchmark")
+    ap.add_argument("--iters", type=int, default=3)
+    args = ap.parse_args()
+    if args.case:
+        run_case(args)
+        return
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)          # rank 0 only; no process group needed
+        return
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -29,6 +29,7 @@
 
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -479,6 +480,12 @@ int4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
     }
 }
 
+}  // namespace convrot
+
+#include "gemm_pair.cuh"
+
+namespace convrot {
+
 // ===========================================================================
 // Host side
 // ===========================================================================
@@ -536,13 +543,58 @@ int launch_gemm(const void* Xp, const void* Wp, const float* xs, const float* ws
     return static_cast<int>(cudaGetLastError());
 }
 
+template <int BN, bool SWAP, int OUT>
+int launch_pair(const void* Xp, const void* Wp, const float* xs, const float* ws, const float* bias,
+                void* out, int M, int N, int K, cudaStream_t stream) {
+    using Cfg = PairCfg<BN>;
+    const void* a_ptr = SWAP ? Wp : Xp;
+    const void* b_ptr = SWAP ? Xp : Wp;
+    const int rows_a = SWAP ? N : M;
+    const int rows_b = SWAP ? M : N;
+    CUtensorMap ta, tb;
+    if (!make_packed_tmap(&ta, a_ptr, rows_a, K, 128) || !make_packed_tmap(&tb, b_ptr, rows_b, K, BN / 2))
+        return fail("cuTensorMapEncodeTiled failed (pointer not 16-byte aligned or driver entry point missing)");
+    auto kernel = int4_gemm_pair_kernel<BN, SWAP, OUT>;
+    cudaError_t e = ensure_smem(kernel, Cfg::kSmemBytes);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * ((rows_a + 255) / 256), (rows_b + BN - 1) / BN, 1);
+    cfg.blockDim = dim3(kPairThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, xs, ws, bias, out, M, N, K);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    return static_cast<int>(cudaGetLastError());
+}
+
+bool force_single_cta_kernel() {
+    static const bool force = [] {
+        const char* v = getenv("CONVROT_GEMM_SINGLE_CTA");
+        return v != nullptr && v[0] == '1';
+    }();
+    return force;
+}
+
 template <int OUT>
 int dispatch_gemm(const void* Xp, const void* Wp, const float* xs, const float* ws, const float* bias,
                   void* out, int M, int N, int K, cudaStream_t stream) {
-    const long tiles256 = static_cast<long>((M + kBM - 1) / kBM) * ((N + 255) / 256);
-    if (N > 128 && tiles256 >= 148)
-        return launch_gemm<256, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
-    return launch_gemm<128, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
+    if (force_single_cta_kernel()) {
+        const long tiles256 = static_cast<long>((M + kBM - 1) / kBM) * ((N + 255) / 256);
+        if (N > 128 && tiles256 >= 148)
+            return launch_gemm<256, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
+        return launch_gemm<128, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
+    }
+    if (M <= 32) return launch_pair<32, true, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
+    if (M <= 64) return launch_pair<64, true, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
+    if (M <= 128) return launch_pair<128, true, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
+    return launch_pair<256, false, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

@@ -295,6 +295,23 @@ def convrot_w4a4_linear(x: np.ndarray, wp: np.ndarray, ws: np.ndarray, bias=None
     return out.astype(np.float16) if dtype == "f16" else out
 
 
+def decode_weight(wp: np.ndarray) -> np.ndarray:
+    """Packed weight [N, K/2] -> its codes as a float32 [N, K] matrix (decode once, reuse)."""
+    return unpack_int4(wp).astype(np.float32)
+
+
+def convrot_w4a4_linear_decoded(x: np.ndarray, w_codes: np.ndarray, ws: np.ndarray, bias=None,
+                                group: int = 256) -> np.ndarray:
+    """``convrot_w4a4_linear`` (bf16) with the weight codes already decoded to float32.
+
+    Same arithmetic: exact integer products (float32 BLAS is exact for these
+    magnitudes), the fp32 epilogue, bf16 output bits.
+    """
+    xp, xs = convrot_quant_int4(x, group, "bf16")
+    acc = unpack_int4(xp).astype(np.float32) @ w_codes.T
+    return int4_gemm_epilogue(acc.astype(np.int32), xs, ws, bias, "bf16")
+
+
 # ---------------------------------------------------------------------------
 # Weight quantization (``_int4/eager.py:49-62``, ``:123-135``), in fp16 like
 # the reference load path (``int4_ops.py:342-349`` casts the weight to fp16)

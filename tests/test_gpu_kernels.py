@@ -113,8 +113,12 @@ def test_fused_quant_vs_reference_eager(ck, case):
 
 # ------------------------------------------------------------------ GEMM
 
+# Covers every kernel variant: swapped (weights in TMEM) for M <= 32/64/128, CTA
+# pairs above; partial k-stages (K/2 not a multiple of 64), tails in M and N,
+# a pair whose second CTA lies wholly outside the matrix.
 GEMM_SHAPES = [(1, 64, 64), (7, 100, 96), (128, 256, 3072), (129, 384, 512), (257, 3072, 3072),
-               (64, 192, 32), (300, 1000, 1024), (512, 3072, 3072), (16, 128, 12288)]
+               (64, 192, 32), (300, 1000, 1024), (512, 3072, 3072), (16, 128, 12288),
+               (33, 520, 160), (100, 300, 224), (65, 18432, 3072), (1, 18432, 3072), (4608, 256, 64)]
 
 
 @pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
