@@ -492,6 +492,8 @@ namespace convrot {
 
 thread_local char g_last_error[256] = "";
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 int fail(const char* msg) {
     snprintf(g_last_error, sizeof(g_last_error), "%s", msg);
     return -1;
@@ -510,16 +512,18 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
     return fn;
 }
 
-// Packed int4 matrix [rows, K/2] bytes, box [box_rows, 64 B], 64-byte swizzle.
-bool make_packed_tmap(CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
+// Packed int4 matrix [rows, K/2] bytes, box [box_rows, box_bytes]; 64- or
+// 128-byte swizzle to match box_bytes.
+bool make_packed_tmap(CUtensorMap* map, const void* base, int rows, int K, int box_rows, int box_bytes = kBKP) {
     auto enc = get_encode_fn();
     if (!enc) return false;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K / 2), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K / 2)};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBKP), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_bytes), static_cast<cuuint32_t>(box_rows)};
     const cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
@@ -543,22 +547,51 @@ int launch_gemm(const void* Xp, const void* Wp, const float* xs, const float* ws
     return static_cast<int>(cudaGetLastError());
 }
 
-template <int BN, bool SWAP, int OUT>
-int launch_pair(const void* Xp, const void* Wp, const float* xs, const float* ws, const float* bias,
-                void* out, int M, int N, int K, cudaStream_t stream) {
-    using Cfg = PairCfg<BN>;
+int sm_count() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 2) return 148;
+    return n;
+}
+
+// bf16 output [M, N] for TMA stores of 128-row x 64-column boxes (128 B swizzle).
+bool make_out_tmap(CUtensorMap* map, void* out, int M, int N) {
+    auto enc = get_encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(N) * 2};
+    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, bool SWAP, int OUT, bool STAGED>
+int launch_pair_impl(const void* Xp, const void* Wp, const float* xs, const float* ws, const float* bias,
+                     void* out, int M, int N, int K, cudaStream_t stream) {
+    using Cfg = PairCfg<BN, STAGED>;
     const void* a_ptr = SWAP ? Wp : Xp;
     const void* b_ptr = SWAP ? Xp : Wp;
     const int rows_a = SWAP ? N : M;
     const int rows_b = SWAP ? M : N;
-    CUtensorMap ta, tb;
-    if (!make_packed_tmap(&ta, a_ptr, rows_a, K, 128) || !make_packed_tmap(&tb, b_ptr, rows_b, K, BN / 2))
+    CUtensorMap ta, tb, to;
+    memset(&to, 0, sizeof(to));
+    if (!make_packed_tmap(&ta, a_ptr, rows_a, K, 128, kPairBKP) ||
+        !make_packed_tmap(&tb, b_ptr, rows_b, K, BN / 2, kPairBKP))
         return fail("cuTensorMapEncodeTiled failed (pointer not 16-byte aligned or driver entry point missing)");
-    auto kernel = int4_gemm_pair_kernel<BN, SWAP, OUT>;
+    if (STAGED && !make_out_tmap(&to, out, M, N))
+        return fail("cuTensorMapEncodeTiled failed for the output");
+    auto kernel = int4_gemm_pair_kernel<BN, SWAP, OUT, STAGED>;
     cudaError_t e = ensure_smem(kernel, Cfg::kSmemBytes);
     if (e != cudaSuccess) return static_cast<int>(e);
+    const int tiles_a = (rows_a + 255) / 256;
+    const int tiles_b = (rows_b + BN - 1) / BN;
+    const long num_tiles = static_cast<long>(tiles_a) * tiles_b;
+    if (num_tiles > 0x7FFFFFFF) return fail("too many output tiles");
+    const int clusters = static_cast<int>(num_tiles < sm_count() / 2 ? num_tiles : sm_count() / 2);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * ((rows_a + 255) / 256), (rows_b + BN - 1) / BN, 1);
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
     cfg.blockDim = dim3(kPairThreads, 1, 1);
     cfg.dynamicSmemBytes = Cfg::kSmemBytes;
     cfg.stream = stream;
@@ -569,9 +602,20 @@ int launch_pair(const void* Xp, const void* Wp, const float* xs, const float* ws
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, xs, ws, bias, out, M, N, K);
+    e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, xs, ws, bias, out, M, N, K, tiles_a,
+                           static_cast<int>(num_tiles));
     if (e != cudaSuccess) return static_cast<int>(e);
     return static_cast<int>(cudaGetLastError());
+}
+
+template <int BN, bool SWAP, int OUT>
+int launch_pair(const void* Xp, const void* Wp, const float* xs, const float* ws, const float* bias,
+                void* out, int M, int N, int K, cudaStream_t stream) {
+    if constexpr (OUT == kOutBF16 && !SWAP) {
+        if ((N % 8) == 0 && aligned16(out))
+            return launch_pair_impl<BN, SWAP, OUT, true>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
+    }
+    return launch_pair_impl<BN, SWAP, OUT, false>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
 }
 
 bool force_single_cta_kernel() {
@@ -596,8 +640,6 @@ int dispatch_gemm(const void* Xp, const void* Wp, const float* xs, const float* 
     if (M <= 128) return launch_pair<128, true, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
     return launch_pair<256, false, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
 }
-
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int check_gemm_args(const void* Xp, const void* Wp, int M, int N, int K) {
     if (M < 0 || N < 0 || K <= 0) return fail("M, N must be >= 0 and K > 0");

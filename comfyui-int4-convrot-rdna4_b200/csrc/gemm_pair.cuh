@@ -1,4 +1,5 @@
-// int4 x int4 GEMM on CTA pairs (tcgen05.mma.cta_group::2.kind::i8, A from TMEM).
+// int4 x int4 GEMM on CTA pairs (tcgen05.mma.cta_group::2.kind::i8, A from TMEM),
+// persistent over output tiles.
 //
 // Included by convrot_b200.cu. Operand roles:
 //   A: 256 rows per CTA pair (128 per CTA), expanded by warps straight into
@@ -15,13 +16,20 @@
 // 256 * (lo_x*lo_w + hi_x*hi_w): the accumulator is 256 * D exactly
 // (|256 * D| <= 256 * 64 * 65536 < 2^31).
 //
-// Warp roles (12 warps, both CTAs alike):
+// Each cluster walks the tiles t = cluster, cluster + clusters, ...; the
+// k-stage ring and all barrier phases run on across tiles, so the loads and
+// expansion of tile i+1 overlap the epilogue of tile i. The epilogue drains
+// the accumulator (into a swizzled shared-memory tile that a TMA store writes
+// out, for bf16 output), then hands TMEM back to the MMA issuer.
+//
+// Warp roles (16 warps, both CTAs alike):
 //   w0        TMA producer (one lane): packed A and B-half tiles per k-stage
 //   w1        TMEM allocation; in the even CTA, one lane issues the MMAs
 //   w2, w3    odd CTA only: forward "stage expanded" to the even CTA, one
 //             cluster-scope release per stage, alternating stages
-//   w4..w7    A expanders (row = 32*(w%4) + lane), then epilogue
-//   w8..w11   B expanders, then epilogue
+//   w4..w7    A expanders (row = 32*(w%4) + lane)
+//   w8..w11   B expanders
+//   w12..w15  epilogue (TMEM lanes 32*(w%4) ..)
 //
 // Stage hand-off: expander warps arrive with CTA-scope release on a local
 // barrier (the MMA's own barrier in the even CTA, a forwarding barrier in the
@@ -32,72 +40,67 @@
 
 namespace convrot {
 
-constexpr int kPairThreads = 12 * 32;
+constexpr int kPairThreads = 16 * 32;
 constexpr uint32_t kTmemCols = 512;
+constexpr int kPairBKP = 128;            // packed bytes of K per stage (256 codes), one 128 B swizzle row
+constexpr int kSwizzle128 = 2;           // tcgen05 descriptor code for 128-byte swizzle
+constexpr int kEpiThreads = 128;         // four epilogue warps
+constexpr uint32_t kEpiBarrier = 1;      // named barrier id of the epilogue warps
 
-template <int BN>
+template <int BN, bool STAGED>
 struct PairCfg {
     static constexpr int kBHalf = BN / 2;
-    static constexpr int kABytes = 128 * kBKP;
-    static constexpr int kBBytes = kBHalf * kBKP;
+    static constexpr int kABytes = 128 * kPairBKP;
+    static constexpr int kBBytes = kBHalf * kPairBKP;
     static constexpr int kStageBytes = kABytes + 2 * kBBytes;
-    static constexpr int kTmemStageCols = 2 * kBKP / 4;          // hi + lo bytes of a row, 4 per column
+    static constexpr int kTmemStageCols = 2 * kPairBKP / 4;      // hi + lo bytes of a row, 4 per column
+    static constexpr int kMmasPerStage = 2 * kPairBKP / 32;        // K = 32 bytes per MMA
+    // bf16 output tile staged for the TMA store: 128 rows x BN cols, 64-col boxes
+    static constexpr int kStagingBytes = STAGED ? 128 * BN * 2 : 0;
+    // 227 KB per block, minus alignment slack, barriers and the staging tile
+    static constexpr int kSmemForStages = 227 * 1024 - 2048 - 4 * BN * 4 - kStagingBytes;
     static constexpr int kStagesByTmem = (static_cast<int>(kTmemCols) - BN) / kTmemStageCols;
-    static constexpr int kStagesBySmem = (192 * 1024) / kStageBytes;
+    static constexpr int kStagesBySmem = kSmemForStages / kStageBytes;
     static constexpr int kStages0 = kStagesByTmem < kStagesBySmem ? kStagesByTmem : kStagesBySmem;
-    static constexpr int kStages = kStages0 < 16 ? kStages0 : 16;
-    static constexpr int kBarOffset = kStages * kStageBytes;
-    static constexpr int kNumBars = 4 * kStages + 1;
+    static constexpr int kStages = kStages0 < 12 ? kStages0 : 12;
+    static constexpr int kStagingOffset = kStages * kStageBytes;
+    static constexpr int kBarOffset = kStagingOffset + kStagingBytes;
+    static constexpr int kNumBars = 4 * kStages + 2;
     static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
-    static constexpr int kColScaleOffset = kMiscOffset + 16;
-    static constexpr int kColBiasOffset = kColScaleOffset + BN * 4;
-    static constexpr int kSmemBytes = kColBiasOffset + BN * 4 + 1024;
+    // per-tile column factors (scale, bias) x 2 tiles in flight
+    static constexpr int kColOffset = kMiscOffset + 16;
+    static constexpr int kSmemBytes = kColOffset + 2 * 2 * BN * 4 + 1024;
     static constexpr uint32_t kIdesc = idesc_i8(256, BN);
     static constexpr int kLocalArrivals = 8;                       // expander warps per CTA
     static constexpr int kReadyCount = kLocalArrivals + 1;         // + the odd CTA's forwarder
     static_assert(BN >= 32 && BN <= 256 && BN % 32 == 0, "pair MMA N must be a multiple of 32 in [32, 256]");
     static_assert(kStages >= 2, "pipeline needs at least two stages");
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
-// Dequantize and store 32 consecutive outputs of one output row (non-swapped
-// layout). v[] holds ((D * xs) * ws) already; bias is added here.
+// Dequantize and store 32 consecutive outputs of one output row directly to
+// global memory. v[] holds ((D * xs) * ws) already; bias is added here.
 template <int OUT>
 __device__ __forceinline__ void store_row32(void* out, size_t obase, int n, int N, float (&v)[32],
                                             const float* bias_cols) {
     const bool full = (n + 32 <= N);
     if constexpr (OUT == kOutBF16) {
-        #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __fadd_rn(v[i], bias_cols[i]);
         __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + obase;
-        if (full && (N & 7) == 0) {
-            #pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-                uint4 pk;
-                __nv_bfloat162 p0 = __floats2bfloat162_rn(v[i], v[i + 1]);
-                __nv_bfloat162 p1 = __floats2bfloat162_rn(v[i + 2], v[i + 3]);
-                __nv_bfloat162 p2 = __floats2bfloat162_rn(v[i + 4], v[i + 5]);
-                __nv_bfloat162 p3 = __floats2bfloat162_rn(v[i + 6], v[i + 7]);
-                memcpy(&pk.x, &p0, 4); memcpy(&pk.y, &p1, 4);
-                memcpy(&pk.z, &p2, 4); memcpy(&pk.w, &p3, 4);
-                *reinterpret_cast<uint4*>(o + i) = pk;
-            }
-        } else {
-            #pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if (n + i < N) o[i] = __float2bfloat16_rn(v[i]);
-        }
-    } else if constexpr (OUT == kOutF32) {
         #pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = __fadd_rn(v[i], bias_cols[i]);
+        for (int i = 0; i < 32; ++i)
+            if (full || n + i < N) o[i] = __float2bfloat16_rn(__fadd_rn(v[i], bias_cols[i]));
+    } else if constexpr (OUT == kOutF32) {
         float* o = reinterpret_cast<float*>(out) + obase;
         if (full && (N & 3) == 0) {
             #pragma unroll
             for (int i = 0; i < 32; i += 4)
-                *reinterpret_cast<float4*>(o + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                *reinterpret_cast<float4*>(o + i) = make_float4(
+                    __fadd_rn(v[i], bias_cols[i]), __fadd_rn(v[i + 1], bias_cols[i + 1]),
+                    __fadd_rn(v[i + 2], bias_cols[i + 2]), __fadd_rn(v[i + 3], bias_cols[i + 3]));
         } else {
             #pragma unroll
             for (int i = 0; i < 32; ++i)
-                if (n + i < N) o[i] = v[i];
+                if (n + i < N) o[i] = __fadd_rn(v[i], bias_cols[i]);
         }
     } else if constexpr (OUT == kOutF32Accumulate) {
         float* o = reinterpret_cast<float*>(out) + obase;
@@ -107,12 +110,17 @@ __device__ __forceinline__ void store_row32(void* out, size_t obase, int n, int 
     }
 }
 
-template <int BN, bool SWAP, int OUT>
+// STAGED (bf16, not swapped, N % 8 == 0): output goes through a shared-memory
+// tile and TMA stores (tmap_out); otherwise the epilogue stores directly.
+template <int BN, bool SWAP, int OUT, bool STAGED>
 __global__ void __launch_bounds__(kPairThreads, 1)
 int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                      const __grid_constant__ CUtensorMap tmap_out,
                       const float* __restrict__ xscale, const float* __restrict__ wscale,
-                      const float* __restrict__ bias, void* __restrict__ out, int M, int N, int K) {
-    using Cfg = PairCfg<BN>;
+                      const float* __restrict__ bias, void* __restrict__ out, int M, int N, int K,
+                      int tiles_a, int num_tiles) {
+    using Cfg = PairCfg<BN, STAGED>;
+    static_assert(!STAGED || (OUT == kOutBF16 && !SWAP), "staged epilogue is for bf16, non-swapped tiles");
     extern __shared__ __align__(1024) unsigned char psmem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(psmem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -121,19 +129,22 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
     uint64_t* ready_bar = bars + Cfg::kStages;
     uint64_t* empty_bar = bars + 2 * Cfg::kStages;
     uint64_t* fwd_bar = bars + 3 * Cfg::kStages;
-    uint64_t* accum_bar = bars + 4 * Cfg::kStages;
+    uint64_t* acc_full_bar = bars + 4 * Cfg::kStages;
+    uint64_t* acc_empty_bar = acc_full_bar + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kMiscOffset);
-    float* col_scale = reinterpret_cast<float*>(smem + Cfg::kColScaleOffset);
-    float* col_bias = reinterpret_cast<float*>(smem + Cfg::kColBiasOffset);
+    unsigned char* staging = smem + Cfg::kStagingOffset;
+    float* col_factors = reinterpret_cast<float*>(smem + Cfg::kColOffset);   // [2][scale BN | bias BN]
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const uint32_t cta = cluster_ctarank();
-    const int a_row0 = (blockIdx.x >> 1) * 256 + static_cast<int>(cta) * 128;
-    const int b_tile0 = blockIdx.y * BN;
-    const int b_row0 = b_tile0 + static_cast<int>(cta) * Cfg::kBHalf;
-    const int num_kt = ((K >> 1) + kBKP - 1) / kBKP;
-    const int rows_b = SWAP ? M : N;
+    const int cluster_id = blockIdx.x >> 1;
+    const int num_clusters = gridDim.x >> 1;
+    const int num_kt = ((K >> 1) + kPairBKP - 1) / kPairBKP;
+    const int rows_a = SWAP ? N : M;
+    // tiles of this cluster, and k-stage iterations over all of them
+    const int my_tiles = (num_tiles - cluster_id + num_clusters - 1) / num_clusters;
+    const int total_it = my_tiles * num_kt;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < Cfg::kStages; ++s) {
@@ -142,28 +153,16 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
             mbar_init(&empty_bar[s], 1);
             mbar_init(&fwd_bar[s], Cfg::kLocalArrivals);
         }
-        mbar_init(accum_bar, 1);
+        mbar_init(acc_full_bar, 1);
+        mbar_init(acc_empty_bar, 2);          // one epilogue arrival from each CTA
         fence_mbar_init();
         tma_prefetch_desc(&tmap_a);
         tma_prefetch_desc(&tmap_b);
+        if constexpr (STAGED) tma_prefetch_desc(&tmap_out);
     }
     if (warp == 1) {
         tmem_alloc_pair(tmem_slot, kTmemCols);
         tmem_relinquish_pair();
-    }
-    if (warp >= 4 && OUT != kOutS32) {
-        // per-column factors of the output tile: B rows are output columns (n)
-        // normally, tokens (m) when swapped
-        for (int c = threadIdx.x - 128; c < BN; c += 256) {
-            const int r = b_tile0 + c;
-            if constexpr (SWAP) {
-                col_scale[c] = (r < rows_b) ? xscale[r] : 0.0f;
-                col_bias[c] = 0.0f;
-            } else {
-                col_scale[c] = (r < rows_b) ? wscale[r] : 0.0f;
-                col_bias[c] = (bias != nullptr && r < rows_b) ? bias[r] : 0.0f;
-            }
-        }
     }
     tc_fence_before();
     cluster_sync();                       // peer barriers initialised before any remote arrive
@@ -173,75 +172,97 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
 
     if (warp == 0) {
         if (lane == 0) {
-            for (int kt = 0; kt < num_kt; ++kt) {
-                const int s = kt % Cfg::kStages;
-                const uint32_t ph = (kt / Cfg::kStages) & 1;
-                if (!mbar_wait_bounded<true>(&empty_bar[s], ph ^ 1)) { record_status(kStatusTimeoutProducer); break; }
-                unsigned char* st = smem + s * Cfg::kStageBytes;
-                mbar_arrive_expect_tx(&full_bar[s], Cfg::kABytes + Cfg::kBBytes);
-                tma_load_2d(st, &tmap_a, &full_bar[s], kt * kBKP, a_row0);
-                tma_load_2d(st + Cfg::kABytes, &tmap_b, &full_bar[s], kt * kBKP, b_row0);
+            // ---------------- TMA producer
+            int it = 0;
+            bool ok = true;
+            for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+                const int a_row0 = (t % tiles_a) * 256 + static_cast<int>(cta) * 128;
+                const int b_row0 = (t / tiles_a) * BN + static_cast<int>(cta) * Cfg::kBHalf;
+                for (int kt = 0; kt < num_kt; ++kt, ++it) {
+                    const int s = it % Cfg::kStages;
+                    const uint32_t ph = (it / Cfg::kStages) & 1;
+                    if (!mbar_wait_bounded<true>(&empty_bar[s], ph ^ 1)) {
+                        record_status(kStatusTimeoutProducer); ok = false; break;
+                    }
+                    unsigned char* st = smem + s * Cfg::kStageBytes;
+                    mbar_arrive_expect_tx(&full_bar[s], Cfg::kABytes + Cfg::kBBytes);
+                    tma_load_2d(st, &tmap_a, &full_bar[s], kt * kPairBKP, a_row0);
+                    tma_load_2d(st + Cfg::kABytes, &tmap_b, &full_bar[s], kt * kPairBKP, b_row0);
+                }
             }
         }
     } else if (warp == 1) {
         if (lane == 0 && cta == 0) {
-            for (int kt = 0; kt < num_kt; ++kt) {
-                const int s = kt % Cfg::kStages;
-                const uint32_t ph = (kt / Cfg::kStages) & 1;
-                if (!mbar_wait_bounded<true>(&ready_bar[s], ph)) { record_status(kStatusTimeoutMma); break; }
-                tc_fence_after();
-                const uint32_t b_hi = smem_u32(smem + s * Cfg::kStageBytes + Cfg::kABytes);
-                #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint32_t b_addr = b_hi + (j >> 1) * Cfg::kBBytes + (j & 1) * 32;
-                    const uint64_t bd = smem_desc_kmajor(b_addr, 8 * kBKP, kSwizzle64);
-                    mma_i8_ts_pair(tmem_base, tmem_a0 + s * Cfg::kTmemStageCols + j * 8, bd, Cfg::kIdesc,
-                                   (kt | j) != 0);
+            // ---------------- MMA issuer (even CTA)
+            int it = 0;
+            bool ok = true;
+            constexpr int kHalfSteps = Cfg::kMmasPerStage / 2;
+            for (int lt = 0; lt < my_tiles && ok; ++lt) {
+                if (lt > 0 && !mbar_wait_bounded<true>(acc_empty_bar, (lt - 1) & 1)) {
+                    record_status(kStatusTimeoutMma); break;
                 }
-                mma_commit_pair_multicast(&empty_bar[s], 0x3);
+                tc_fence_after();
+                for (int kt = 0; kt < num_kt; ++kt, ++it) {
+                    const int s = it % Cfg::kStages;
+                    const uint32_t ph = (it / Cfg::kStages) & 1;
+                    if (!mbar_wait_bounded<true>(&ready_bar[s], ph)) {
+                        record_status(kStatusTimeoutMma); ok = false; break;
+                    }
+                    tc_fence_after();
+                    const uint32_t b_hi = smem_u32(smem + s * Cfg::kStageBytes + Cfg::kABytes);
+                    #pragma unroll
+                    for (int j = 0; j < Cfg::kMmasPerStage; ++j) {
+                        const uint32_t b_addr = b_hi + (j / kHalfSteps) * Cfg::kBBytes + (j % kHalfSteps) * 32;
+                        const uint64_t bd = smem_desc_kmajor(b_addr, 8 * kPairBKP, kSwizzle128);
+                        mma_i8_ts_pair(tmem_base, tmem_a0 + s * Cfg::kTmemStageCols + j * 8, bd, Cfg::kIdesc,
+                                       (kt | j) != 0);
+                    }
+                    mma_commit_pair_multicast(&empty_bar[s], 0x3);
+                }
+                if (ok) mma_commit_pair_multicast(acc_full_bar, 0x3);
             }
-            mma_commit_pair_multicast(accum_bar, 0x3);
         }
     } else if (warp < 4) {
         if (cta == 1 && lane == 0) {
             // ---------------- forwarders (odd CTA): local expansion done -> even CTA's MMA barrier
             const uint32_t ready_leader0 = mapa_shared(smem_u32(&ready_bar[0]), 0);
-            for (int kt = warp - 2; kt < num_kt; kt += 2) {
-                const int s = kt % Cfg::kStages;
-                const uint32_t ph = (kt / Cfg::kStages) & 1;
+            for (int it = warp - 2; it < total_it; it += 2) {
+                const int s = it % Cfg::kStages;
+                const uint32_t ph = (it / Cfg::kStages) & 1;
                 if (!mbar_wait_bounded(&fwd_bar[s], ph)) { record_status(kStatusTimeoutExpand); break; }
                 mbar_arrive_cluster(ready_leader0 + s * 8);
             }
         }
-    } else {
+    } else if (warp < 12) {
         // expansion done for stage s: local arrive (CTA-scope release)
         uint64_t* done_bar = (cta == 0) ? ready_bar : fwd_bar;
         const int quarter = warp & 3;
-        bool ok = true;
         if (warp < 8) {
             // ---------------- A expanders: one row per thread, into TMEM
             const int r = quarter * 32 + lane;
-            const uint32_t swz = static_cast<uint32_t>((r >> 1) & 3);
-            for (int kt = 0; kt < num_kt; ++kt) {
-                const int s = kt % Cfg::kStages;
-                const uint32_t ph = (kt / Cfg::kStages) & 1;
+            const uint32_t swz = static_cast<uint32_t>(r & 7);   // 128 B swizzle: chunk ^= row % 8
+            for (int it = 0; it < total_it; ++it) {
+                const int s = it % Cfg::kStages;
+                const uint32_t ph = (it / Cfg::kStages) & 1;
                 if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&full_bar[s], ph))) {
-                    record_status(kStatusTimeoutExpand); ok = false; break;
+                    record_status(kStatusTimeoutExpand); break;
                 }
-                const unsigned char* row = smem + s * Cfg::kStageBytes + r * kBKP;
-                uint32_t w[32];
+                const unsigned char* row = smem + s * Cfg::kStageBytes + r * kPairBKP;
+                uint32_t hi[32], lo[32];
                 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
+                for (int c = 0; c < 8; ++c) {
                     const uint4 v = *reinterpret_cast<const uint4*>(row + ((c ^ swz) << 4));
                     const uint32_t p[4] = {v.x, v.y, v.z, v.w};
                     #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        w[4 * c + e] = p[e] & 0xF0F0F0F0u;
-                        w[16 + 4 * c + e] = (p[e] << 4) & 0xF0F0F0F0u;
+                        hi[4 * c + e] = p[e] & 0xF0F0F0F0u;
+                        lo[4 * c + e] = (p[e] << 4) & 0xF0F0F0F0u;
                     }
                 }
+                const uint32_t ta = tmem_a0 + (static_cast<uint32_t>(quarter * 32) << 16) + s * Cfg::kTmemStageCols;
                 __syncwarp();
-                tmem_st_32x32b_x32(tmem_a0 + (static_cast<uint32_t>(quarter * 32) << 16) + s * Cfg::kTmemStageCols, w);
+                tmem_st_32x32b_x32(ta, hi);
+                tmem_st_32x32b_x32(ta + 32, lo);
                 tmem_st_wait();
                 tc_fence_before();
                 __syncwarp();
@@ -250,11 +271,11 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         } else {
             // ---------------- B expanders: in place (high) + second buffer (low)
             const int et = threadIdx.x - 256;
-            for (int kt = 0; kt < num_kt; ++kt) {
-                const int s = kt % Cfg::kStages;
-                const uint32_t ph = (kt / Cfg::kStages) & 1;
+            for (int it = 0; it < total_it; ++it) {
+                const int s = it % Cfg::kStages;
+                const uint32_t ph = (it / Cfg::kStages) & 1;
                 if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&full_bar[s], ph))) {
-                    record_status(kStatusTimeoutExpand); ok = false; break;
+                    record_status(kStatusTimeoutExpand); break;
                 }
                 uint4* hi = reinterpret_cast<uint4*>(smem + s * Cfg::kStageBytes + Cfg::kABytes);
                 uint4* lo = reinterpret_cast<uint4*>(smem + s * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes);
@@ -274,17 +295,21 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                 if (lane == 0) mbar_arrive(&done_bar[s]);
             }
         }
-
-        // ---------------- epilogue: this CTA's 128 accumulator lanes x BN columns
-        ok = __all_sync(0xFFFFFFFFu, ok && mbar_wait_bounded<true>(accum_bar, 0));
-        if (!ok && lane == 0) record_status(kStatusTimeoutEpilogue);
-        tc_fence_after();
-        constexpr bool kSplitCols = BN >= 64;
-        constexpr int kColsPerWarp = kSplitCols ? BN / 2 : BN;
-        const int col_half = (warp - 4) >> 2;
-        if (kSplitCols || col_half == 0) {
-            const int a = a_row0 + quarter * 32 + lane;          // A row of this lane
-            const bool lane_ok = ok && a < (SWAP ? N : M);
+    } else {
+        // ---------------- epilogue: this CTA's 128 accumulator lanes x BN columns, per tile
+        const int quarter = warp & 3;
+        const int et = threadIdx.x - 384;                       // 0..127
+        const int r = quarter * 32 + lane;                      // row within the CTA tile
+        const uint32_t acc_empty_leader = mapa_shared(smem_u32(acc_empty_bar), 0);
+        for (int lt = 0; lt < my_tiles; ++lt) {
+            const int t = cluster_id + lt * num_clusters;
+            const int a_row0 = (t % tiles_a) * 256 + static_cast<int>(cta) * 128;
+            const int b_tile0 = (t / tiles_a) * BN;
+            const int a = a_row0 + r;                                // A row of this lane
+            const bool lane_ok = a < rows_a;
+            // Per-tile factors, fetched while the tile's MMAs still run: the lane's
+            // row factor in a register, the BN column factors into shared memory
+            // (read back as warp-wide broadcasts).
             float lane_scale = 0.0f, lane_bias = 0.0f;
             if (lane_ok && OUT != kOutS32) {
                 if constexpr (SWAP) {
@@ -294,49 +319,122 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                     lane_scale = xscale[a];
                 }
             }
-            #pragma unroll 1
-            for (int cc = 0; cc < kColsPerWarp / 32; ++cc) {
-                const int col0 = col_half * kColsPerWarp + cc * 32;
-                uint32_t r[32];
-                __syncwarp();
-                tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + col0, r);
-                tmem_ld_wait();
-                if (!lane_ok) continue;
-                const int b = b_tile0 + col0;                       // first B row of this chunk
-                if constexpr (OUT == kOutS32) {
-                    #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const int32_t d = static_cast<int32_t>(r[i]) >> 8;
-                        if constexpr (SWAP) {
-                            if (b + i < M) reinterpret_cast<int32_t*>(out)[static_cast<size_t>(b + i) * N + a] = d;
-                        } else {
-                            if (b + i < N) reinterpret_cast<int32_t*>(out)[static_cast<size_t>(a) * N + b + i] = d;
-                        }
+            float* cscale = col_factors + (lt & 1) * (2 * BN);
+            float* cbias = cscale + BN;
+            if constexpr (OUT != kOutS32) {
+                for (int c = et; c < BN; c += kEpiThreads) {
+                    const int n = b_tile0 + c;
+                    if constexpr (SWAP) {
+                        cscale[c] = (n < M) ? xscale[n] : 0.0f;
+                        cbias[c] = 0.0f;
+                    } else {
+                        cscale[c] = (n < N) ? wscale[n] : 0.0f;
+                        cbias[c] = (bias != nullptr && n < N) ? bias[n] : 0.0f;
                     }
-                } else if constexpr (SWAP) {
-                    #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        if (b + i >= M) break;
-                        const float d = static_cast<float>(static_cast<int32_t>(r[i]) >> 8);
-                        const float v = __fmul_rn(__fmul_rn(d, col_scale[col0 + i]), lane_scale);
-                        const size_t o = static_cast<size_t>(b + i) * N + a;
-                        if constexpr (OUT == kOutBF16)
-                            reinterpret_cast<__nv_bfloat16*>(out)[o] = __float2bfloat16_rn(__fadd_rn(v, lane_bias));
-                        else if constexpr (OUT == kOutF32)
-                            reinterpret_cast<float*>(out)[o] = __fadd_rn(v, lane_bias);
-                        else
-                            reinterpret_cast<float*>(out)[o] = __fadd_rn(reinterpret_cast<float*>(out)[o], v);
-                    }
-                } else {
-                    float v[32];
-                    #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const float d = static_cast<float>(static_cast<int32_t>(r[i]) >> 8);
-                        v[i] = __fmul_rn(__fmul_rn(d, lane_scale), col_scale[col0 + i]);
-                    }
-                    store_row32<OUT>(out, static_cast<size_t>(a) * N + b, b, N, v, col_bias + col0);
                 }
             }
+            if constexpr (STAGED) {
+                // the previous tile's TMA stores must have read the staging tile
+                if (et == 0) bulk_wait_group_read0();
+            }
+            named_barrier_sync(kEpiBarrier, kEpiThreads);
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded<true>(acc_full_bar, lt & 1))) {
+                if (lane == 0) record_status(kStatusTimeoutEpilogue);
+                break;
+            }
+            tc_fence_after();
+            #pragma unroll 1
+            for (int cc = 0; cc < BN / 32; cc += 2) {
+                // two 32-column TMEM loads in flight per wait
+                uint32_t acc2[2][32];
+                __syncwarp();
+                const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + cc * 32;
+                tmem_ld_32x32b_x32(taddr, acc2[0]);
+                tmem_ld_32x32b_x32(taddr + 32, acc2[1]);
+                tmem_ld_wait();
+                #pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t (&acc)[32] = acc2[h];
+                    const int col0 = (cc + h) * 32;
+                    const int b = b_tile0 + col0;                    // first B row of this chunk
+                    if constexpr (OUT == kOutS32) {
+                        if (!lane_ok) continue;
+                        #pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const int32_t d = static_cast<int32_t>(acc[i]) >> 8;
+                            if constexpr (SWAP) {
+                                if (b + i < M) reinterpret_cast<int32_t*>(out)[static_cast<size_t>(b + i) * N + a] = d;
+                            } else {
+                                if (b + i < N) reinterpret_cast<int32_t*>(out)[static_cast<size_t>(a) * N + b + i] = d;
+                            }
+                        }
+                    } else if constexpr (SWAP) {
+                        if (!lane_ok) continue;
+                        #pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            if (b + i >= M) break;
+                            const float d = static_cast<float>(static_cast<int32_t>(acc[i]) >> 8);
+                            const float v = __fmul_rn(__fmul_rn(d, cscale[col0 + i]), lane_scale);
+                            const size_t o = static_cast<size_t>(b + i) * N + a;
+                            if constexpr (OUT == kOutBF16)
+                                reinterpret_cast<__nv_bfloat16*>(out)[o] = __float2bfloat16_rn(__fadd_rn(v, lane_bias));
+                            else if constexpr (OUT == kOutF32)
+                                reinterpret_cast<float*>(out)[o] = __fadd_rn(v, lane_bias);
+                            else
+                                reinterpret_cast<float*>(out)[o] = __fadd_rn(reinterpret_cast<float*>(out)[o], v);
+                        }
+                    } else {
+                        float v[32];
+                        #pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const float d = static_cast<float>(static_cast<int32_t>(acc[i]) >> 8);
+                            v[i] = __fmul_rn(__fmul_rn(d, lane_scale), cscale[col0 + i]);
+                        }
+                        if constexpr (STAGED) {
+                            // 32 bf16 = four 16-byte chunks of a 64-column, 128 B-swizzled box
+                            unsigned char* box = staging + (col0 >> 6) * (128 * 128);
+                            const int c0 = (col0 & 63) >> 3;
+                            #pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                uint4 pk;
+                                const float* bq = cbias + col0 + 8 * q;
+                                __nv_bfloat162 p0 = __floats2bfloat162_rn(__fadd_rn(v[8 * q], bq[0]),
+                                                                          __fadd_rn(v[8 * q + 1], bq[1]));
+                                __nv_bfloat162 p1 = __floats2bfloat162_rn(__fadd_rn(v[8 * q + 2], bq[2]),
+                                                                          __fadd_rn(v[8 * q + 3], bq[3]));
+                                __nv_bfloat162 p2 = __floats2bfloat162_rn(__fadd_rn(v[8 * q + 4], bq[4]),
+                                                                          __fadd_rn(v[8 * q + 5], bq[5]));
+                                __nv_bfloat162 p3 = __floats2bfloat162_rn(__fadd_rn(v[8 * q + 6], bq[6]),
+                                                                          __fadd_rn(v[8 * q + 7], bq[7]));
+                                memcpy(&pk.x, &p0, 4); memcpy(&pk.y, &p1, 4);
+                                memcpy(&pk.z, &p2, 4); memcpy(&pk.w, &p3, 4);
+                                *reinterpret_cast<uint4*>(box + r * 128 + (((c0 + q) ^ (r & 7)) << 4)) = pk;
+                            }
+                        } else {
+                            if (!lane_ok) continue;
+                            store_row32<OUT>(out, static_cast<size_t>(a) * N + b, b, N, v, cbias + col0);
+                        }
+                    }
+                }
+            }
+            // accumulator drained: hand TMEM back to the MMA issuer
+            tc_fence_before();
+            if constexpr (STAGED) fence_proxy_async_smem();
+            named_barrier_sync(kEpiBarrier, kEpiThreads);
+            if (et == 0) {
+                if (cta == 0) mbar_arrive(acc_empty_bar);
+                else mbar_arrive_cluster(acc_empty_leader);
+                if constexpr (STAGED) {
+                    for (int bx = 0; bx < BN / 64; ++bx) {
+                        if (b_tile0 + bx * 64 < N && a_row0 < M)
+                            tma_store_2d(&tmap_out, staging + bx * (128 * 128), b_tile0 + bx * 64, a_row0);
+                    }
+                    bulk_commit_group();
+                }
+            }
+        }
+        if constexpr (STAGED) {
+            if (et == 0) bulk_wait_group0();
         }
     }
 

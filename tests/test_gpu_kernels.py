@@ -132,7 +132,10 @@ def test_gemm_int32_accumulators_exact(ck, m, n, k):
     assert np.array_equal(to_storage(acc).astype(np.int64), xi @ wi.T)
 
 
-@pytest.mark.parametrize("m,n,k", [(1, 64, 64), (77, 300, 1024), (256, 512, 3072), (200, 3072, 12288)])
+# (2048, 3072): more output tiles than CTA pairs on the GPU (persistent tile loop);
+# (515, 2056): staged bf16 stores with tails in M and in the last 64-column box.
+@pytest.mark.parametrize("m,n,k", [(1, 64, 64), (77, 300, 1024), (256, 512, 3072), (200, 3072, 12288),
+                                   (2048, 3072, 256), (515, 2056, 320)])
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("with_bias", [True, False])
 def test_gemm_epilogue_bit_exact(ck, m, n, k, out_dtype, with_bias):
