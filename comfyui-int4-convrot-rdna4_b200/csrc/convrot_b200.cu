@@ -109,7 +109,7 @@ template <typename T>
 __device__ __forceinline__ void load16(const T* p, float (&v)[16]) {
     if constexpr (sizeof(T) == 2) {
         const uint4* q = reinterpret_cast<const uint4*>(p);
-        uint4 a = __ldg(q), b = __ldg(q + 1);
+        uint4 a = q[0], b = q[1];
         const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
         #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -124,128 +124,334 @@ __device__ __forceinline__ void load16(const T* p, float (&v)[16]) {
         const float4* q = reinterpret_cast<const float4*>(p);
         #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            float4 a = __ldg(q + i);
+            float4 a = q[i];
             v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = a.z; v[4 * i + 3] = a.w;
         }
     }
 }
 
 constexpr int kQuantThreads = 256;
-constexpr int kTransposeFloats = 16 * 16 * 17;   // 16 half-warps x 16 x 17 (padded)
+constexpr int kTrStride = 20;                        // floats per transposed row (16 + pad, 16 B aligned)
+constexpr int kTransposeFloats = 16 * 16 * kTrStride; // 16 half-warps x 16 x 20
 
-// One block handles `rows_per_block` rows. Phase 1: each half-warp rotates
-// 256-element tiles (a 16x16 matrix, element i = 16a + b): H16 along b in
-// registers, a padded shared-memory transpose, then H_{G/16} along a; the
-// result is rounded to the activation dtype, kept in a shared row buffer and
-// folded into the row absmax. Phase 2: per-row scale. Phase 3: quantize and
-// pack 16 elements per step into 8 output bytes.
-// G == 1 skips the rotation (the input is already rotated).
-template <typename T, int G>
+// 16x16 transpose of 4-bit codes held by the 16 lanes of a half-warp. On entry
+// lane b holds column b of a tile, nibble a (bits 4a..4a+3 of the 64-bit word
+// {lo, hi}) = element (a, b); on exit lane t holds row t, nibble b = element
+// (t, b) -- which, read as 8 little-endian bytes, is the packed int4 row
+// (column 2c in the low nibble of byte c). Four butterfly exchanges with the
+// lane at distance 8, 4, 2, 1, each swapping the half of the word whose
+// nibble-index bit differs from the lane's bit.
+__device__ __forceinline__ void transpose_nibbles16(uint32_t& lo, uint32_t& hi, int j, unsigned hmask) {
+    // distance 8: nibbles 8..15 are the high word
+    {
+        const bool up = j & 8;
+        const uint32_t got = __shfl_xor_sync(hmask, up ? lo : hi, 8);
+        if (up) lo = got; else hi = got;
+    }
+    // distance 4: nibbles with bit 2 set are the upper 16 bits of each word
+    {
+        const bool up = j & 4;
+        const uint32_t send = up ? __byte_perm(lo, hi, 0x5410) : __byte_perm(lo, hi, 0x7632);
+        const uint32_t got = __shfl_xor_sync(hmask, send, 4);
+        if (up) { lo = __byte_perm(lo, got, 0x3254); hi = __byte_perm(hi, got, 0x3276); }
+        else    { lo = __byte_perm(lo, got, 0x5410); hi = __byte_perm(hi, got, 0x7610); }
+    }
+    // distance 2: nibbles with bit 1 set are the odd bytes of each word
+    {
+        const bool up = j & 2;
+        const uint32_t send = up ? __byte_perm(lo, hi, 0x6420) : __byte_perm(lo, hi, 0x7531);
+        const uint32_t got = __shfl_xor_sync(hmask, send, 2);
+        if (up) { lo = __byte_perm(lo, got, 0x3514); hi = __byte_perm(hi, got, 0x3716); }
+        else    { lo = __byte_perm(lo, got, 0x5240); hi = __byte_perm(hi, got, 0x7260); }
+    }
+    // distance 1: nibbles with bit 0 set are the high nibbles of each byte
+    {
+        const bool up = j & 1;
+        const uint32_t send = up ? ((lo & 0x0F0F0F0Fu) | ((hi & 0x0F0F0F0Fu) << 4))
+                                 : (((lo >> 4) & 0x0F0F0F0Fu) | (hi & 0xF0F0F0F0u));
+        const uint32_t got = __shfl_xor_sync(hmask, send, 1);
+        if (up) { lo = (lo & 0xF0F0F0F0u) | (got & 0x0F0F0F0Fu); hi = (hi & 0xF0F0F0F0u) | ((got >> 4) & 0x0F0F0F0Fu); }
+        else    { lo = (lo & 0x0F0F0F0Fu) | ((got & 0x0F0F0F0Fu) << 4); hi = (hi & 0x0F0F0F0Fu) | (got & 0xF0F0F0F0u); }
+    }
+}
+
+// ---- paired fp32 arithmetic (sm_100 f32x2): one instruction for two independent lanes of work
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
+// h4 on two tiles at once (same arithmetic as h4(), per component).
+__device__ __forceinline__ void h4x2(float2& v0, float2& v1, float2& v2, float2& v3) {
+    const float2 m2 = make_float2(-2.0f, -2.0f);
+    const float2 s = add2(add2(v0, v1), add2(v2, v3));
+    const float2 o0 = fma2(m2, v3, s), o1 = fma2(m2, v2, s), o2 = fma2(m2, v1, s), o3 = fma2(m2, v0, s);
+    v0 = o0; v1 = o1; v2 = o2; v3 = o3;
+}
+__device__ __forceinline__ void h16x2(float2 (&v)[16]) {
+    #pragma unroll
+    for (int hi = 0; hi < 4; ++hi) h4x2(v[4 * hi], v[4 * hi + 1], v[4 * hi + 2], v[4 * hi + 3]);
+    #pragma unroll
+    for (int lo = 0; lo < 4; ++lo) h4x2(v[lo], v[lo + 4], v[lo + 8], v[lo + 12]);
+}
+__device__ __forceinline__ void h4_low_digit_x2(float2 (&v)[16]) {
+    #pragma unroll
+    for (int hi = 0; hi < 4; ++hi) h4x2(v[4 * hi], v[4 * hi + 1], v[4 * hi + 2], v[4 * hi + 3]);
+}
+
+// Rounded rotated values of two tiles, as kept until the row scale is known:
+// 16-bit dtypes packed two per register (tile 2p in the low half), f32 as is.
+template <typename T> struct PairStore {
+    using type = uint32_t;
+    __device__ static type pack(float2 v) {
+        if constexpr (Act<T>::kCode == 1) {
+            __nv_bfloat162 b = __floats2bfloat162_rn(v.x, v.y);
+            uint32_t u; memcpy(&u, &b, 4); return u;
+        } else {
+            __half2 h = __floats2half2_rn(v.x, v.y);
+            uint32_t u; memcpy(&u, &h, 4); return u;
+        }
+    }
+    __device__ static float2 unpack(type u) {
+        if constexpr (Act<T>::kCode == 1) {
+            return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
+        } else {
+            __half2 h; memcpy(&h, &u, 4); return __half22float2(h);
+        }
+    }
+};
+template <> struct PairStore<float> {
+    using type = float2;
+    __device__ static type pack(float2 v) { return v; }
+    __device__ static float2 unpack(type v) { return v; }
+};
+
+// 4-bit two's-complement code of y (a value of the activation dtype) divided
+// by the row scale, with the eager quantizer's roundings (generic path).
+template <typename T>
+__device__ __forceinline__ uint32_t quant_nibble(float y, float s) {
+    float qf = rintf(Act<T>::round(__fdiv_rn(y, s)));
+    qf = fminf(fmaxf(qf, -7.0f), 7.0f);
+    return static_cast<uint32_t>(static_cast<int>(qf)) & 0xFu;
+}
+
+// bf16 codes of two values: t = bf16(fp32(y * fp32(1/s))), which equals
+// bf16(fp32(y / s)) for bf16 y and s; |t| <= 7 * (1 + 2^-8) < 7.5, so no clamp
+// is needed; adding 1.5 * 2^23 rounds t half-to-even to an integer held in the
+// low mantissa bits, whose low nibble is the two's-complement code.
+__device__ __forceinline__ void quant_pair_bf16(float2 y, float2 rcp, uint32_t& n0, uint32_t& n1) {
+    const float2 t = mul2(y, rcp);
+    __nv_bfloat162 b = __floats2bfloat162_rn(t.x, t.y);
+    uint32_t u; memcpy(&u, &b, 4);
+    const float2 tb = make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
+    const float2 r = add2(tb, make_float2(12582912.0f, 12582912.0f));
+    n0 = __float_as_uint(r.x) & 0xFu;
+    n1 = __float_as_uint(r.y) & 0xFu;
+}
+
+// Persistent: block b handles the row groups b, b + gridDim.x, ... of
+// `rows_per_block` rows each. A group's rows are contiguous in memory and
+// arrive by one bulk copy into a double-buffered shared-memory slab, issued
+// two groups ahead, so HBM streams while the block computes.
+// Within a group, half-warp h owns tiles h, h+16, ... (at most MAXT, MAXT
+// even). A tile is 256 consecutive elements of a row seen as a 16x16 matrix
+// (i = 16a + b); lane j of the half-warp takes row a = j. Tiles are processed
+// in pairs so every butterfly step is one paired-fp32 instruction. Rotation:
+// H16 along b in registers, a padded shared-memory transpose (lane j now
+// holds column b = j), then H16 (G=256) or H4 on the low digit of a (G=64),
+// scale 1/sqrt(G), round to the activation dtype. After the row absmax
+// (shared atomics) the codes are formed in registers and put back in row
+// order with transpose_nibbles16. G == 16 needs no transform along a and
+// G == 1 (pre-rotated input) none at all: those keep lane j on row a = j.
+template <typename T, int G, int MAXT>
 __global__ void __launch_bounds__(kQuantThreads)
 convrot_quant_kernel(const T* __restrict__ x, int8_t* __restrict__ qout, float* __restrict__ scaleout,
                      int M, int K, int rows_per_block) {
+    static_assert(MAXT % 2 == 0, "tiles are processed in pairs");
+    constexpr int NP = MAXT / 2;
+    constexpr bool kColumnLayout = (G == 64 || G == 256);
     extern __shared__ __align__(16) unsigned char qsmem[];
     float* tr = reinterpret_cast<float*>(qsmem);                               // transpose scratch
     uint32_t* rowmax = reinterpret_cast<uint32_t*>(tr + kTransposeFloats);     // [rows_per_block]
     float* row_scale = reinterpret_cast<float*>(rowmax + rows_per_block);      // [rows_per_block]
     float* row_rcp = row_scale + rows_per_block;                                // [rows_per_block]
-    T* rowbuf = reinterpret_cast<T*>(qsmem + (((kTransposeFloats + 3 * rows_per_block) * 4 + 15) & ~15));
+    uint64_t* full = reinterpret_cast<uint64_t*>(
+        qsmem + ((static_cast<size_t>(kTransposeFloats + 3 * rows_per_block) * 4 + 15) & ~static_cast<size_t>(15)));
+    const size_t slab_elems = static_cast<size_t>(rows_per_block) * K;
+    T* slab = reinterpret_cast<T*>(reinterpret_cast<unsigned char*>(full) + 16 + 112);   // 128 B in
+    // slab[0 .. slab_elems) and slab[slab_elems .. 2 * slab_elems): the two buffers
 
-    const int row0 = blockIdx.x * rows_per_block;
-    const int nrows = min(rows_per_block, M - row0);
     const int tid = threadIdx.x;
-    for (int r = tid; r < nrows; r += kQuantThreads) rowmax[r] = 0u;
+    const int groups = (M + rows_per_block - 1) / rows_per_block;
+    auto issue = [&](int g, int b) {
+        const int r0 = g * rows_per_block;
+        const int nr = min(rows_per_block, M - r0);
+        const uint32_t bytes = static_cast<uint32_t>(static_cast<size_t>(nr) * K * sizeof(T));
+        mbar_arrive_expect_tx(&full[b], bytes);
+        bulk_load(slab + b * slab_elems, x + static_cast<size_t>(r0) * K, bytes, &full[b]);
+    };
+    if (tid == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        fence_mbar_init();
+    }
+    for (int r = tid; r < rows_per_block; r += kQuantThreads) rowmax[r] = 0u;
     __syncthreads();
+    if (tid == 0) {
+        if (blockIdx.x < groups) issue(blockIdx.x, 0);
+        if (blockIdx.x + gridDim.x < groups) issue(blockIdx.x + gridDim.x, 1);
+    }
 
     const int hw = tid >> 4;          // half-warp 0..15
     const int j = tid & 15;           // lane within the half-warp
     const unsigned hmask = 0xFFFFu << (16 * ((tid & 31) >> 4));
     const int ntile = (K + 255) >> 8;
-    float* my_tr = tr + hw * (16 * 17);
+    float* my_tr = tr + hw * (16 * kTrStride);
 
-    for (int t = hw; t < nrows * ntile; t += 16) {
-        const int r = t / ntile;
-        const int tile = t - r * ntile;
-        const int kbase = tile * 256;
-        const int valid_rows = min(16, (K - kbase) >> 4);      // rows a of this tile inside K
-        const T* src = x + static_cast<size_t>(row0 + r) * K + kbase;
-        T* dst = rowbuf + static_cast<size_t>(r) * K + kbase;
-        float v[16];
-        if (j < valid_rows) load16<T>(src + 16 * j, v);
-        else {
+    int trow[MAXT], tkb[MAXT];
+    #pragma unroll
+    for (int i = 0; i < MAXT; ++i) {
+        const int g = hw + 16 * i;
+        trow[i] = g / ntile;
+        tkb[i] = (g - trow[i] * ntile) * 256;
+    }
+
+    int it = 0;
+    for (int grp = blockIdx.x; grp < groups; grp += gridDim.x, ++it) {
+        const int buf = it & 1;
+        const int row0 = grp * rows_per_block;
+        const int nrows = min(rows_per_block, M - row0);
+        const int my_tiles = max(0, (nrows * ntile - hw + 15) >> 4);   // tiles of this half-warp (<= MAXT)
+        auto row_valid = [&](int i) { return i < my_tiles && 16 * j < K - tkb[i]; };
+        if (!mbar_wait_bounded(&full[buf], (it >> 1) & 1)) { record_status(kStatusTimeoutExpand); break; }
+        const T* src = slab + buf * slab_elems;
+
+        // ---- this lane's rows of its tiles, from the slab
+        float2 v[NP][16];
+        #pragma unroll
+        for (int p = 0; p < NP; ++p) {
+            float a0[16], a1[16];
             #pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+            for (int e = 0; e < 16; ++e) { a0[e] = 0.0f; a1[e] = 0.0f; }
+            if (row_valid(2 * p)) load16<T>(src + static_cast<size_t>(trow[2 * p]) * K + tkb[2 * p] + 16 * j, a0);
+            if (row_valid(2 * p + 1))
+                load16<T>(src + static_cast<size_t>(trow[2 * p + 1]) * K + tkb[2 * p + 1] + 16 * j, a1);
+            #pragma unroll
+            for (int e = 0; e < 16; ++e) v[p][e] = make_float2(a0[e], a1[e]);
         }
-        float m = 0.0f;
-        if constexpr (G == 1) {
-            if (j < valid_rows) {
+        __syncthreads();                  // slab buffer consumed: refill it two groups ahead
+        if (tid == 0 && grp + 2 * static_cast<int>(gridDim.x) < groups) issue(grp + 2 * gridDim.x, buf);
+
+        // ---- rotate and round in place, two tiles per pass; row absmax through shared atomics
+        #pragma unroll
+        for (int p = 0; p < NP; ++p) {
+            if (2 * p >= my_tiles) break;
+            if constexpr (G != 1) h16x2(v[p]);                    // along b
+            if constexpr (kColumnLayout) {
                 #pragma unroll
-                for (int b = 0; b < 16; ++b) {
-                    m = fmaxf(m, fabsf(v[b]));
-                    dst[16 * j + b] = Act<T>::from_f32(v[b]);
+                for (int h = 0; h < 2; ++h) {
+                    #pragma unroll
+                    for (int b = 0; b < 16; ++b) my_tr[b * kTrStride + j] = h ? v[p][b].y : v[p][b].x;
+                    __syncwarp(hmask);
+                    #pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float4 c = *reinterpret_cast<const float4*>(my_tr + j * kTrStride + 4 * q);
+                        if (h) { v[p][4 * q].y = c.x; v[p][4 * q + 1].y = c.y; v[p][4 * q + 2].y = c.z; v[p][4 * q + 3].y = c.w; }
+                        else   { v[p][4 * q].x = c.x; v[p][4 * q + 1].x = c.y; v[p][4 * q + 2].x = c.z; v[p][4 * q + 3].x = c.w; }
+                    }
+                    __syncwarp(hmask);
                 }
+                if constexpr (G == 256) h16x2(v[p]);              // along a
+                else h4_low_digit_x2(v[p]);                       // along a0 (groups of 4 rows)
             }
-        } else {
-            h16(v);                                      // along b
+            float m0 = 0.0f, m1 = 0.0f;
+            constexpr float kNorm = (G == 256) ? 0.0625f : (G == 64) ? 0.125f : (G == 16) ? 0.25f : 1.0f;
             #pragma unroll
-            for (int b = 0; b < 16; ++b) my_tr[j * 17 + b] = v[b];
-            __syncwarp(hmask);
-            float w[16];
+            for (int e = 0; e < 16; ++e) {
+                float2 sc = v[p][e];
+                if constexpr (G != 1) sc = mul2(sc, make_float2(kNorm, kNorm));
+                v[p][e] = make_float2(Act<T>::round(sc.x), Act<T>::round(sc.y));
+                m0 = fmaxf(m0, fabsf(v[p][e].x));
+                m1 = fmaxf(m1, fabsf(v[p][e].y));
+            }
             #pragma unroll
-            for (int a = 0; a < 16; ++a) w[a] = my_tr[a * 17 + j];
-            __syncwarp(hmask);
-            if constexpr (G == 256) h16(w);              // along a
-            else if constexpr (G == 64) h4_low_digit(w); // along a0 only (groups of 4 rows)
-            constexpr float kNorm = (G == 256) ? 0.0625f : (G == 64) ? 0.125f : 0.25f;
-            #pragma unroll
-            for (int a = 0; a < 16; ++a) {
-                if (a < valid_rows) {
-                    const float y = Act<T>::round(__fmul_rn(w[a], kNorm));
-                    m = fmaxf(m, fabsf(y));
-                    dst[16 * a + j] = Act<T>::from_f32(y);
-                }
+            for (int off = 8; off > 0; off >>= 1) {
+                m0 = fmaxf(m0, __shfl_xor_sync(hmask, m0, off));
+                m1 = fmaxf(m1, __shfl_xor_sync(hmask, m1, off));
+            }
+            if (j == 0) {
+                atomicMax(&rowmax[trow[2 * p]], __float_as_uint(m0));
+                if (2 * p + 1 < my_tiles) atomicMax(&rowmax[trow[2 * p + 1]], __float_as_uint(m1));
             }
         }
-        #pragma unroll
-        for (int off = 8; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(hmask, m, off));
-        if (j == 0) atomicMax(&rowmax[r], __float_as_uint(m));
-    }
-    __syncthreads();
+        __syncthreads();
 
-    for (int r = tid; r < nrows; r += kQuantThreads) {
-        const float amax = fmaxf(__uint_as_float(rowmax[r]), Act<T>::floor_value());
-        const float s = Act<T>::round(__fdiv_rn(amax, 7.0f));
-        row_scale[r] = s;
-        row_rcp[r] = __frcp_rn(s);
-        scaleout[row0 + r] = s;
-    }
-    __syncthreads();
+        for (int r = tid; r < nrows; r += kQuantThreads) {
+            const float amax = fmaxf(__uint_as_float(rowmax[r]), Act<T>::floor_value());
+            const float s = Act<T>::round(__fdiv_rn(amax, 7.0f));
+            row_scale[r] = s;
+            row_rcp[r] = __frcp_rn(s);
+            scaleout[row0 + r] = s;
+            rowmax[r] = 0u;               // ready for the next group
+        }
+        __syncthreads();
 
-    const int steps_per_row = K >> 4;
-    for (int c = tid; c < nrows * steps_per_row; c += kQuantThreads) {
-        const int r = c / steps_per_row;
-        const int k0 = (c - r * steps_per_row) << 4;
-        const T* src = rowbuf + static_cast<size_t>(r) * K + k0;
-        const float s = row_scale[r];
-        const float rcp = row_rcp[r];
-        uint32_t packed[2] = {0u, 0u};
+        // ---- codes, back in row order, 8 output bytes per lane and tile
         #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const float y = Act<T>::to_f32(src[i]);
-            float tq;
+        for (int p = 0; p < NP; ++p) {
+            if (2 * p >= my_tiles) break;
+            const int r0 = trow[2 * p];
+            const int r1 = (2 * p + 1 < my_tiles) ? trow[2 * p + 1] : r0;
+            uint32_t lo0 = 0u, hi0 = 0u, lo1 = 0u, hi1 = 0u;
             if constexpr (Act<T>::kCode == 1) {
-                // For bf16 y and s, bf16(fp32(y * fp32(1/s))) == bf16(fp32(y / s)).
-                tq = Act<T>::round(__fmul_rn(y, rcp));
+                const float2 rcp = make_float2(row_rcp[r0], row_rcp[r1]);
+                #pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    uint32_t n0, n1;
+                    quant_pair_bf16(v[p][e], rcp, n0, n1);
+                    if (e < 8) { lo0 |= n0 << (4 * e); lo1 |= n1 << (4 * e); }
+                    else       { hi0 |= n0 << (4 * (e - 8)); hi1 |= n1 << (4 * (e - 8)); }
+                }
             } else {
-                tq = Act<T>::round(__fdiv_rn(y, s));
+                const float s0 = row_scale[r0], s1 = row_scale[r1];
+                #pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const uint32_t n0 = quant_nibble<T>(v[p][e].x, s0), n1 = quant_nibble<T>(v[p][e].y, s1);
+                    if (e < 8) { lo0 |= n0 << (4 * e); lo1 |= n1 << (4 * e); }
+                    else       { hi0 |= n0 << (4 * (e - 8)); hi1 |= n1 << (4 * (e - 8)); }
+                }
             }
-            float qf = rintf(tq);
-            qf = fminf(fmaxf(qf, -7.0f), 7.0f);
-            const uint32_t nib = static_cast<uint32_t>(static_cast<int>(qf)) & 0xFu;
-            packed[i >> 3] |= nib << (4 * (i & 7));
+            if constexpr (kColumnLayout) {
+                transpose_nibbles16(lo0, hi0, j, hmask);
+                transpose_nibbles16(lo1, hi1, j, hmask);
+            }
+            #pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int i = 2 * p + h;
+                if (row_valid(i)) {
+                    uint2* dst = reinterpret_cast<uint2*>(qout + static_cast<size_t>(row0 + trow[i]) * (K >> 1) +
+                                                          (tkb[i] >> 1) + 8 * j);
+                    *dst = h ? make_uint2(lo1, hi1) : make_uint2(lo0, hi0);
+                }
+            }
         }
-        uint2* out = reinterpret_cast<uint2*>(qout + static_cast<size_t>(row0 + r) * (K >> 1) + (k0 >> 1));
-        *out = make_uint2(packed[0], packed[1]);
     }
 }
 
@@ -494,6 +700,14 @@ thread_local char g_last_error[256] = "";
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+int sm_count() {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 2) return 148;
+    return n;
+}
+
+
 int fail(const char* msg) {
     snprintf(g_last_error, sizeof(g_last_error), "%s", msg);
     return -1;
@@ -545,13 +759,6 @@ int launch_gemm(const void* Xp, const void* Wp, const float* xs, const float* ws
     dim3 grid((N + BN - 1) / BN, (M + kBM - 1) / kBM);
     kernel<<<grid, kGemmThreads, GemmCfg<BN>::kSmemBytes, stream>>>(tx, tw, xs, ws, bias, out, M, N, K);
     return static_cast<int>(cudaGetLastError());
-}
-
-int sm_count() {
-    int dev = 0, n = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 2) return 148;
-    return n;
 }
 
 // bf16 output [M, N] for TMA stores of 128-row x 64-column boxes (128 B swizzle).
@@ -653,16 +860,25 @@ int check_gemm_args(const void* Xp, const void* Wp, int M, int N, int K) {
 template <typename T, int G>
 int launch_quant_t(const void* x, void* q, void* s, int M, int K, cudaStream_t stream) {
     const int ntile = (K + 255) / 256;
-    int rows = 48 / ntile;
-    rows = rows < 1 ? 1 : (rows > 64 ? 64 : rows);
+    // at most MAXT tiles per half-warp: 16 half-warps x MAXT tiles per row group
+    const bool big = ntile > 64;
+    const int maxt = big ? 16 : 4;
+    int rows = (16 * maxt) / ntile;
+    rows = rows < 1 ? 1 : rows;
     if (rows > M) rows = M;
-    const size_t head = ((kTransposeFloats + 3 * rows) * 4 + 15) & ~static_cast<size_t>(15);
-    const size_t bytes = head + static_cast<size_t>(rows) * K * sizeof(T);
-    if (bytes > 227 * 1024) return fail("row too long for the shared-memory row buffer");
-    auto kernel = convrot_quant_kernel<T, G>;
+    if (static_cast<long>(rows) * ntile > 16L * maxt) return fail("row too long for the quantizer");
+    const size_t head = ((static_cast<size_t>(kTransposeFloats) + 3 * rows) * 4 + 15) & ~static_cast<size_t>(15);
+    const size_t bytes = head + 128 + 2 * static_cast<size_t>(rows) * K * sizeof(T);
+    if (bytes > 227 * 1024) return fail("row too long for the quantizer's shared-memory slabs");
+    auto kernel = big ? convrot_quant_kernel<T, G, 16> : convrot_quant_kernel<T, G, 4>;
     cudaError_t e = ensure_smem(kernel, static_cast<int>(bytes));
     if (e != cudaSuccess) return static_cast<int>(e);
-    const int grid = (M + rows - 1) / rows;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kQuantThreads, bytes);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    const int groups = (M + rows - 1) / rows;
+    const int resident = sm_count() * (per_sm > 0 ? per_sm : 1);
+    const int grid = groups < resident ? groups : resident;
     kernel<<<grid, kQuantThreads, bytes, stream>>>(static_cast<const T*>(x), static_cast<int8_t*>(q),
                                                   static_cast<float*>(s), M, K, rows);
     return static_cast<int>(cudaGetLastError());

@@ -288,3 +288,14 @@ __device__ __forceinline__ void named_barrier_sync(uint32_t id, uint32_t nthread
 }
 
 }  // namespace convrot
+
+namespace convrot {
+
+// Contiguous bulk copy global -> shared (this CTA), completion on `bar`.
+// Addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+}  // namespace convrot
