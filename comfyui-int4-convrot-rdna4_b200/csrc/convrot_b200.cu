@@ -777,7 +777,7 @@ bool make_out_tmap(CUtensorMap* map, void* out, int M, int N) {
 template <int BN, bool SWAP, int OUT, bool STAGED>
 int launch_pair_impl(const void* Xp, const void* Wp, const float* xs, const float* ws, const float* bias,
                      void* out, int M, int N, int K, cudaStream_t stream) {
-    using Cfg = PairCfg<BN, STAGED>;
+    using Cfg = PairCfg<BN, STAGED, SWAP>;
     const void* a_ptr = SWAP ? Wp : Xp;
     const void* b_ptr = SWAP ? Xp : Wp;
     const int rows_a = SWAP ? N : M;
@@ -845,6 +845,10 @@ int dispatch_gemm(const void* Xp, const void* Wp, const float* xs, const float* 
     if (M <= 32) return launch_pair<32, true, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
     if (M <= 64) return launch_pair<64, true, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
     if (M <= 128) return launch_pair<128, true, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
+    // 256x256 pair tiles unless that leaves more than half of the CTA pairs idle
+    const long tiles256 = static_cast<long>((M + 255) / 256) * ((N + 255) / 256);
+    if (2 * tiles256 < sm_count() / 2)
+        return launch_pair<128, false, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
     return launch_pair<256, false, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
 }
 

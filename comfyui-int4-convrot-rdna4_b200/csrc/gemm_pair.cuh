@@ -47,7 +47,7 @@ constexpr int kSwizzle128 = 2;           // tcgen05 descriptor code for 128-byte
 constexpr int kEpiThreads = 128;         // four epilogue warps
 constexpr uint32_t kEpiBarrier = 1;      // named barrier id of the epilogue warps
 
-template <int BN, bool STAGED>
+template <int BN, bool STAGED, bool SWAP>
 struct PairCfg {
     static constexpr int kBHalf = BN / 2;
     static constexpr int kABytes = 128 * kPairBKP;
@@ -59,22 +59,27 @@ struct PairCfg {
     static constexpr int kStagingBytes = STAGED ? 128 * BN * 2 : 0;
     // 227 KB per block, minus alignment slack, barriers and the staging tile
     static constexpr int kSmemForStages = 227 * 1024 - 2048 - 4 * BN * 4 - kStagingBytes;
-    static constexpr int kStagesByTmem = (static_cast<int>(kTmemCols) - BN) / kTmemStageCols;
+    // TMA ring (shared memory) and expanded-A ring (TMEM slots) are sized
+    // independently: the loads may run further ahead than TMEM allows.
+    static constexpr int kTmemStages0 = (static_cast<int>(kTmemCols) - BN) / kTmemStageCols;
     static constexpr int kStagesBySmem = kSmemForStages / kStageBytes;
-    static constexpr int kStages0 = kStagesByTmem < kStagesBySmem ? kStagesByTmem : kStagesBySmem;
-    static constexpr int kStages = kStages0 < 12 ? kStages0 : 12;
+    static constexpr int kStages = kStagesBySmem < 16 ? kStagesBySmem : 16;
+    static constexpr int kTmemStages = kTmemStages0 < kStages ? kTmemStages0 : kStages;
     static constexpr int kStagingOffset = kStages * kStageBytes;
     static constexpr int kBarOffset = kStagingOffset + kStagingBytes;
-    static constexpr int kNumBars = 4 * kStages + 2;
+    static constexpr int kNumBars = 4 * kStages + kTmemStages + 2;
     static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
     // per-tile column factors (scale, bias) x 2 tiles in flight
     static constexpr int kColOffset = kMiscOffset + 16;
     static constexpr int kSmemBytes = kColOffset + 2 * 2 * BN * 4 + 1024;
     static constexpr uint32_t kIdesc = idesc_i8(256, BN);
-    static constexpr int kLocalArrivals = 8;                       // expander warps per CTA
+    // swapped (weight-bound) tiles: three groups of four warps take turns on
+    // whole stages (A and B), otherwise four A and four B expander warps
+    static constexpr int kExpGroups = SWAP ? 3 : 1;
+    static constexpr int kLocalArrivals = SWAP ? 4 : 8;            // expander warps per CTA and stage
     static constexpr int kReadyCount = kLocalArrivals + 1;         // + the odd CTA's forwarder
     static_assert(BN >= 32 && BN <= 256 && BN % 32 == 0, "pair MMA N must be a multiple of 32 in [32, 256]");
-    static_assert(kStages >= 2, "pipeline needs at least two stages");
+    static_assert(kStages >= 2 && kTmemStages >= 2, "pipeline needs at least two stages");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -119,7 +124,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                       const float* __restrict__ xscale, const float* __restrict__ wscale,
                       const float* __restrict__ bias, void* __restrict__ out, int M, int N, int K,
                       int tiles_a, int num_tiles) {
-    using Cfg = PairCfg<BN, STAGED>;
+    using Cfg = PairCfg<BN, STAGED, SWAP>;
     static_assert(!STAGED || (OUT == kOutBF16 && !SWAP), "staged epilogue is for bf16, non-swapped tiles");
     extern __shared__ __align__(1024) unsigned char psmem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -129,7 +134,8 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
     uint64_t* ready_bar = bars + Cfg::kStages;
     uint64_t* empty_bar = bars + 2 * Cfg::kStages;
     uint64_t* fwd_bar = bars + 3 * Cfg::kStages;
-    uint64_t* acc_full_bar = bars + 4 * Cfg::kStages;
+    uint64_t* tmem_free_bar = bars + 4 * Cfg::kStages;           // [kTmemStages]
+    uint64_t* acc_full_bar = tmem_free_bar + Cfg::kTmemStages;
     uint64_t* acc_empty_bar = acc_full_bar + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kMiscOffset);
     unsigned char* staging = smem + Cfg::kStagingOffset;
@@ -153,6 +159,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
             mbar_init(&empty_bar[s], 1);
             mbar_init(&fwd_bar[s], Cfg::kLocalArrivals);
         }
+        for (int t = 0; t < Cfg::kTmemStages; ++t) mbar_init(&tmem_free_bar[t], 1);
         mbar_init(acc_full_bar, 1);
         mbar_init(acc_empty_bar, 2);          // one epilogue arrival from each CTA
         fence_mbar_init();
@@ -210,14 +217,16 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                     }
                     tc_fence_after();
                     const uint32_t b_hi = smem_u32(smem + s * Cfg::kStageBytes + Cfg::kABytes);
+                    const int ts = it % Cfg::kTmemStages;
                     #pragma unroll
                     for (int j = 0; j < Cfg::kMmasPerStage; ++j) {
                         const uint32_t b_addr = b_hi + (j / kHalfSteps) * Cfg::kBBytes + (j % kHalfSteps) * 32;
                         const uint64_t bd = smem_desc_kmajor(b_addr, 8 * kPairBKP, kSwizzle128);
-                        mma_i8_ts_pair(tmem_base, tmem_a0 + s * Cfg::kTmemStageCols + j * 8, bd, Cfg::kIdesc,
+                        mma_i8_ts_pair(tmem_base, tmem_a0 + ts * Cfg::kTmemStageCols + j * 8, bd, Cfg::kIdesc,
                                        (kt | j) != 0);
                     }
                     mma_commit_pair_multicast(&empty_bar[s], 0x3);
+                    mma_commit_pair_multicast(&tmem_free_bar[ts], 0x3);
                 }
                 if (ok) mma_commit_pair_multicast(acc_full_bar, 0x3);
             }
@@ -233,69 +242,104 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                 mbar_arrive_cluster(ready_leader0 + s * 8);
             }
         }
-    } else if (warp < 12) {
+    } else if (warp < 12 || SWAP) {
         // expansion done for stage s: local arrive (CTA-scope release)
         uint64_t* done_bar = (cta == 0) ? ready_bar : fwd_bar;
         const int quarter = warp & 3;
-        if (warp < 8) {
-            // ---------------- A expanders: one row per thread, into TMEM
+        // A rows into TMEM: one row (128 packed bytes) per thread
+        auto expand_a = [&](int s, int ts) {
             const int r = quarter * 32 + lane;
             const uint32_t swz = static_cast<uint32_t>(r & 7);   // 128 B swizzle: chunk ^= row % 8
+            const unsigned char* row = smem + s * Cfg::kStageBytes + r * kPairBKP;
+            uint32_t hi[32], lo[32];
+            #pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                const uint4 v = *reinterpret_cast<const uint4*>(row + ((c ^ swz) << 4));
+                const uint32_t p[4] = {v.x, v.y, v.z, v.w};
+                #pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    hi[4 * c + e] = p[e] & 0xF0F0F0F0u;
+                    lo[4 * c + e] = (p[e] << 4) & 0xF0F0F0F0u;
+                }
+            }
+            const uint32_t ta = tmem_a0 + (static_cast<uint32_t>(quarter * 32) << 16) + ts * Cfg::kTmemStageCols;
+            __syncwarp();
+            tmem_st_32x32b_x32(ta, hi);
+            tmem_st_32x32b_x32(ta + 32, lo);
+            tmem_st_wait();
+            tc_fence_before();
+        };
+        // B half tile: in place (high) + second buffer (low), by `nthr` threads
+        auto expand_b = [&](int s, int et, int nthr) {
+            uint4* hi = reinterpret_cast<uint4*>(smem + s * Cfg::kStageBytes + Cfg::kABytes);
+            uint4* lo = reinterpret_cast<uint4*>(smem + s * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes);
+            for (int c = et; c < Cfg::kBBytes / 16; c += nthr) {
+                const uint4 v = hi[c];
+                uint4 h, l;
+                h.x = v.x & 0xF0F0F0F0u; l.x = (v.x << 4) & 0xF0F0F0F0u;
+                h.y = v.y & 0xF0F0F0F0u; l.y = (v.y << 4) & 0xF0F0F0F0u;
+                h.z = v.z & 0xF0F0F0F0u; l.z = (v.z << 4) & 0xF0F0F0F0u;
+                h.w = v.w & 0xF0F0F0F0u; l.w = (v.w << 4) & 0xF0F0F0F0u;
+                hi[c] = h;
+                lo[c] = l;
+            }
+            fence_proxy_async_smem();
+        };
+        if constexpr (SWAP) {
+            // ---------------- three groups of four warps, whole stages in turn
+            const int group = (warp - 4) >> 2;
+            const int et = (warp & 3) * 32 + lane;
+            for (int it = group; it < total_it; it += Cfg::kExpGroups) {
+                const int s = it % Cfg::kStages;
+                const uint32_t ph = (it / Cfg::kStages) & 1;
+                if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&full_bar[s], ph))) {
+                    record_status(kStatusTimeoutExpand); break;
+                }
+                const int ts = it % Cfg::kTmemStages;
+                if (!__all_sync(0xFFFFFFFFu,
+                                mbar_wait_bounded<true>(&tmem_free_bar[ts], ((it / Cfg::kTmemStages) & 1) ^ 1))) {
+                    record_status(kStatusTimeoutExpand); break;
+                }
+                tc_fence_after();
+                expand_a(s, ts);
+                expand_b(s, et, 128);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&done_bar[s]);
+            }
+        } else if (warp < 8) {
+            // ---------------- A expanders
             for (int it = 0; it < total_it; ++it) {
                 const int s = it % Cfg::kStages;
                 const uint32_t ph = (it / Cfg::kStages) & 1;
                 if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&full_bar[s], ph))) {
                     record_status(kStatusTimeoutExpand); break;
                 }
-                const unsigned char* row = smem + s * Cfg::kStageBytes + r * kPairBKP;
-                uint32_t hi[32], lo[32];
-                #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const uint4 v = *reinterpret_cast<const uint4*>(row + ((c ^ swz) << 4));
-                    const uint32_t p[4] = {v.x, v.y, v.z, v.w};
-                    #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        hi[4 * c + e] = p[e] & 0xF0F0F0F0u;
-                        lo[4 * c + e] = (p[e] << 4) & 0xF0F0F0F0u;
-                    }
+                const int ts = it % Cfg::kTmemStages;
+                if (!__all_sync(0xFFFFFFFFu,
+                                mbar_wait_bounded<true>(&tmem_free_bar[ts], ((it / Cfg::kTmemStages) & 1) ^ 1))) {
+                    record_status(kStatusTimeoutExpand); break;
                 }
-                const uint32_t ta = tmem_a0 + (static_cast<uint32_t>(quarter * 32) << 16) + s * Cfg::kTmemStageCols;
-                __syncwarp();
-                tmem_st_32x32b_x32(ta, hi);
-                tmem_st_32x32b_x32(ta + 32, lo);
-                tmem_st_wait();
-                tc_fence_before();
+                tc_fence_after();
+                expand_a(s, ts);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&done_bar[s]);
             }
         } else {
-            // ---------------- B expanders: in place (high) + second buffer (low)
-            const int et = threadIdx.x - 256;
+            // ---------------- B expanders
             for (int it = 0; it < total_it; ++it) {
                 const int s = it % Cfg::kStages;
                 const uint32_t ph = (it / Cfg::kStages) & 1;
                 if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&full_bar[s], ph))) {
                     record_status(kStatusTimeoutExpand); break;
                 }
-                uint4* hi = reinterpret_cast<uint4*>(smem + s * Cfg::kStageBytes + Cfg::kABytes);
-                uint4* lo = reinterpret_cast<uint4*>(smem + s * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes);
-                #pragma unroll
-                for (int c = et; c < Cfg::kBBytes / 16; c += 128) {
-                    const uint4 v = hi[c];
-                    uint4 h, l;
-                    h.x = v.x & 0xF0F0F0F0u; l.x = (v.x << 4) & 0xF0F0F0F0u;
-                    h.y = v.y & 0xF0F0F0F0u; l.y = (v.y << 4) & 0xF0F0F0F0u;
-                    h.z = v.z & 0xF0F0F0F0u; l.z = (v.z << 4) & 0xF0F0F0F0u;
-                    h.w = v.w & 0xF0F0F0F0u; l.w = (v.w << 4) & 0xF0F0F0F0u;
-                    hi[c] = h;
-                    lo[c] = l;
-                }
-                fence_proxy_async_smem();
+                expand_b(s, threadIdx.x - 256, 128);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&done_bar[s]);
             }
         }
-    } else {
+    }
+    if (warp >= 12) {
+        // (with SWAP these warps also took their turns as expanders above)
         // ---------------- epilogue: this CTA's 128 accumulator lanes x BN columns, per tile
         const int quarter = warp & 3;
         const int et = threadIdx.x - 384;                       // 0..127
