@@ -1,9 +1,8 @@
 """Generate the golden vectors in this folder from the reference's own eager code.
 
-Run in a container that has the reference checkout (default path below, or
-``--reference PATH``)::
+Run where the reference checkout is available::
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --reference PATH_TO_REFERENCE_CHECKOUT
 
 It imports the reference package ``_int4`` (eager.py, _codec.py) directly from
 its source tree under a private module name and runs its CPU torch functions on
@@ -30,7 +29,6 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-DEFAULT_REF = "/root/reference"
 
 
 def load_reference(path: str):
@@ -66,7 +64,7 @@ def activation(gen: torch.Generator, m: int, k: int, outlier_frac: float = 0.01)
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=DEFAULT_REF)
+    ap.add_argument("--reference", required=True, help="root of the reference project checkout")
     args = ap.parse_args()
     ref = load_reference(args.reference)
     eager, codec = ref.eager, ref._codec
