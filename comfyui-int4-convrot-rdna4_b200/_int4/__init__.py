@@ -18,7 +18,7 @@ from __future__ import annotations
 import torch
 
 from ._codec import _INT4_GROUP_SIZE
-from .cuda_loader import convrot_quant_int4, int4_convrot_gemm
+from .cuda_loader import convrot_quant_int4, int4_convrot_gemm, int4_convrot_gemm_lora
 from .cuda_loader import is_available as _lib_available
 from .eager import (
     _build_hadamard,
@@ -34,6 +34,7 @@ __all__ = [
     "dequantize_convrot_w4a4_weight",
     "convrot_w4a4_linear",
     "convrot_w8a8_linear",
+    "convrot_w4a4_linear_lora",
     "is_available",
     "pick_groupsize",
 ]
@@ -98,6 +99,58 @@ def convrot_w4a4_linear(
     qact, x_scale = convrot_quant_int4(x2d, convrot_groupsize)
     out_dtype = x.dtype if x.dtype in _NATIVE_OUT else torch.float32
     out = int4_convrot_gemm(qact, qweight, x_scale, wscales, bias, out_dtype)
+    if out.dtype != x.dtype:
+        out = out.to(x.dtype)
+    return out.reshape(*shape[:-1], qweight.shape[0])
+
+
+_MAX_LORA_RANK = 64
+
+
+def convrot_w4a4_linear_lora(
+    x: torch.Tensor,
+    qweight: torch.Tensor,
+    wscales: torch.Tensor,
+    bias: torch.Tensor | None,
+    adapters,
+    convrot_groupsize: int = 256,
+) -> torch.Tensor:
+    """``convrot_w4a4_linear`` plus Dynamic-LoRA side paths fused into the GEMM epilogue.
+
+    adapters: iterable of (down [r, K], up [N, r], scale) with scale = (alpha / r) * strength,
+    the low-rank "bypass" of the node's forward (int4_ops.py:181-192). The down
+    projection T = x @ down^T runs as one bf16 GEMM; the up projection and the add
+    run on the tensor cores inside the int4 GEMM, before the single output
+    rounding. Several adapters are stacked along the rank (total rank <= 64); with
+    more than one, each scale is folded into its up matrix in bf16.
+    """
+    adapters = list(adapters)
+    if not adapters:
+        return convrot_w4a4_linear(x, qweight, wscales, bias, convrot_groupsize)
+    _validate(x, qweight, convrot_groupsize, _INT4_GROUP_SIZE, "int4")
+    shape = x.shape
+    x2d = x.reshape(-1, shape[-1]).contiguous()
+    if len(adapters) == 1:
+        down, up, scale = adapters[0]
+        down = down.to(device=x.device, dtype=torch.bfloat16)
+        up = up.to(device=x.device, dtype=torch.bfloat16)
+    else:
+        down = torch.cat([d.to(device=x.device, dtype=torch.bfloat16) for d, _, _ in adapters], dim=0)
+        up = torch.cat([(u.to(device=x.device, dtype=torch.float32) * float(s)).to(torch.bfloat16)
+                        for _, u, s in adapters], dim=1)
+        scale = 1.0
+    rank = down.shape[0]
+    if rank > _MAX_LORA_RANK or up.shape != (qweight.shape[0], rank) or down.shape[1] != shape[-1]:
+        raise ValueError(f"LoRA down {tuple(down.shape)} / up {tuple(up.shape)} do not fit this layer "
+                         f"(total rank must be <= {_MAX_LORA_RANK})")
+    pad = (-rank) % 8
+    if pad:
+        down = torch.nn.functional.pad(down, (0, 0, 0, pad))
+        up = torch.nn.functional.pad(up, (0, pad))
+    lora_t = x2d.to(torch.bfloat16) @ down.t()
+    qact, x_scale = convrot_quant_int4(x2d, convrot_groupsize)
+    out_dtype = x.dtype if x.dtype in _NATIVE_OUT else torch.float32
+    out = int4_convrot_gemm_lora(qact, qweight, x_scale, wscales, bias, out_dtype, lora_t, up, scale)
     if out.dtype != x.dtype:
         out = out.to(x.dtype)
     return out.reshape(*shape[:-1], qweight.shape[0])

@@ -28,6 +28,7 @@ _SIGNATURES = {
     "ck_int4_quant_rowwise": [_P, _I, _P, _P, _I, _I, _P],
     "ck_int4_convrot_gemm": [_P] * 6 + [_I] * 4 + [_P],
     "ck_int4_convrot_gemm_splitk": [_P] * 5 + [_I] * 4 + [_P],
+    "ck_int4_convrot_gemm_lora": [_P] * 6 + [_I] * 4 + [_P, _P, _I, ctypes.c_float, _P],
     "ck_int4_gemm_s32": [_P, _P, _P, _I, _I, _I, _P],
     "ck_convrot_device_status": [_P, ctypes.POINTER(ctypes.c_int)],
     "ck_convrot_last_error": [],
@@ -138,6 +139,36 @@ def int4_convrot_gemm(x_packed, w_packed, x_scale, w_scale, bias, out_dtype):
                                   w_scale.data_ptr(), bias_ptr, out.data_ptr(), m, n, k,
                                   _OUT_DTYPE_CODE[out_dtype], _stream(x_packed))
     _check("ck_int4_convrot_gemm", rc)
+    return out
+
+
+def int4_convrot_gemm_lora(x_packed, w_packed, x_scale, w_scale, bias, out_dtype, lora_t, lora_b, lora_scale):
+    """int4_convrot_gemm plus lora_scale * (lora_t @ lora_b^T), fused in the epilogue.
+
+    lora_t: bf16 [M, r] (= x @ A^T), lora_b: bf16 [N, r], r a multiple of 8 up to 64.
+    """
+    lib = _load()
+    if out_dtype not in _OUT_DTYPE_CODE:
+        raise ValueError(f"int4 gemm output dtype must be float32/bfloat16, got {out_dtype}")
+    x_packed, w_packed, m, n, k = _packed_pair(x_packed, w_packed)
+    _require_cuda(lora_t, lora_b)
+    lora_t = lora_t.to(torch.bfloat16).contiguous()
+    lora_b = lora_b.to(torch.bfloat16).contiguous()
+    r = lora_t.shape[1]
+    if tuple(lora_t.shape) != (m, r) or tuple(lora_b.shape) != (n, r):
+        raise ValueError(f"LoRA shapes {tuple(lora_t.shape)} / {tuple(lora_b.shape)} do not match M={m}, N={n}")
+    x_scale = x_scale.to(torch.float32).contiguous()
+    w_scale = w_scale.to(torch.float32).contiguous()
+    out = torch.empty((m, n), dtype=out_dtype, device=x_packed.device)
+    bias_ptr = 0
+    if bias is not None:
+        bias = bias.to(torch.float32).contiguous()
+        bias_ptr = bias.data_ptr()
+    rc = lib.ck_int4_convrot_gemm_lora(x_packed.data_ptr(), w_packed.data_ptr(), x_scale.data_ptr(),
+                                       w_scale.data_ptr(), bias_ptr, out.data_ptr(), m, n, k,
+                                       _OUT_DTYPE_CODE[out_dtype], lora_t.data_ptr(), lora_b.data_ptr(), r,
+                                       float(lora_scale), _stream(x_packed))
+    _check("ck_int4_convrot_gemm_lora", rc)
     return out
 
 

@@ -774,22 +774,47 @@ bool make_out_tmap(CUtensorMap* map, void* out, int M, int N) {
                CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, bool SWAP, int OUT, bool STAGED>
+// bf16 matrix [rows, cols] (row-major) read in boxes of 64 columns x box_rows, 128 B swizzle.
+bool make_bf16_tmap(CUtensorMap* map, const void* base, int rows, int cols, int box_rows) {
+    auto enc = get_encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct LoraArgs {
+    const void* t = nullptr;      // bf16 [M, rank]
+    const void* b = nullptr;      // bf16 [N, rank]
+    int rank = 0;
+    float scale = 0.0f;
+};
+
+template <int BN, bool SWAP, int OUT, bool STAGED, bool LORA>
 int launch_pair_impl(const void* Xp, const void* Wp, const float* xs, const float* ws, const float* bias,
-                     void* out, int M, int N, int K, cudaStream_t stream) {
-    using Cfg = PairCfg<BN, STAGED, SWAP>;
+                     void* out, int M, int N, int K, const LoraArgs& lora, cudaStream_t stream) {
+    using Cfg = PairCfg<BN, STAGED, SWAP, LORA>;
     const void* a_ptr = SWAP ? Wp : Xp;
     const void* b_ptr = SWAP ? Xp : Wp;
     const int rows_a = SWAP ? N : M;
     const int rows_b = SWAP ? M : N;
-    CUtensorMap ta, tb, to;
+    CUtensorMap ta, tb, to, tlt, tlb;
     memset(&to, 0, sizeof(to));
+    memset(&tlt, 0, sizeof(tlt));
+    memset(&tlb, 0, sizeof(tlb));
     if (!make_packed_tmap(&ta, a_ptr, rows_a, K, 128, kPairBKP) ||
         !make_packed_tmap(&tb, b_ptr, rows_b, K, BN / 2, kPairBKP))
         return fail("cuTensorMapEncodeTiled failed (pointer not 16-byte aligned or driver entry point missing)");
     if (STAGED && !make_out_tmap(&to, out, M, N))
         return fail("cuTensorMapEncodeTiled failed for the output");
-    auto kernel = int4_gemm_pair_kernel<BN, SWAP, OUT, STAGED>;
+    if (LORA && (!make_bf16_tmap(&tlt, lora.t, M, lora.rank, 128) ||
+                 !make_bf16_tmap(&tlb, lora.b, N, lora.rank, BN / 2)))
+        return fail("cuTensorMapEncodeTiled failed for the LoRA operands");
+    auto kernel = int4_gemm_pair_kernel<BN, SWAP, OUT, STAGED, LORA>;
     cudaError_t e = ensure_smem(kernel, Cfg::kSmemBytes);
     if (e != cudaSuccess) return static_cast<int>(e);
     const int tiles_a = (rows_a + 255) / 256;
@@ -809,20 +834,20 @@ int launch_pair_impl(const void* Xp, const void* Wp, const float* xs, const floa
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, xs, ws, bias, out, M, N, K, tiles_a,
-                           static_cast<int>(num_tiles));
+    e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, tlt, tlb, xs, ws, bias, out, M, N, K, tiles_a,
+                           static_cast<int>(num_tiles), lora.scale);
     if (e != cudaSuccess) return static_cast<int>(e);
     return static_cast<int>(cudaGetLastError());
 }
 
-template <int BN, bool SWAP, int OUT>
+template <int BN, bool SWAP, int OUT, bool LORA = false>
 int launch_pair(const void* Xp, const void* Wp, const float* xs, const float* ws, const float* bias,
-                void* out, int M, int N, int K, cudaStream_t stream) {
+                void* out, int M, int N, int K, cudaStream_t stream, const LoraArgs& lora = LoraArgs()) {
     if constexpr (OUT == kOutBF16 && !SWAP) {
         if ((N % 8) == 0 && aligned16(out))
-            return launch_pair_impl<BN, SWAP, OUT, true>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
+            return launch_pair_impl<BN, SWAP, OUT, true, LORA>(Xp, Wp, xs, ws, bias, out, M, N, K, lora, stream);
     }
-    return launch_pair_impl<BN, SWAP, OUT, false>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
+    return launch_pair_impl<BN, SWAP, OUT, false, LORA>(Xp, Wp, xs, ws, bias, out, M, N, K, lora, stream);
 }
 
 bool force_single_cta_kernel() {
@@ -949,6 +974,30 @@ CONVROT_API int ck_int4_convrot_gemm(const void* Xp, const void* Wp, const void*
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (out_dtype == 1) return dispatch_gemm<kOutBF16>(Xp, Wp, xs, ws, b, out, M, N, K, s);
     return dispatch_gemm<kOutF32>(Xp, Wp, xs, ws, b, out, M, N, K, s);
+}
+
+CONVROT_API int ck_int4_convrot_gemm_lora(const void* Xp, const void* Wp, const void* xscale, const void* wscale,
+                                          const void* bias, void* out, int M, int N, int K, int out_dtype,
+                                          const void* lora_t, const void* lora_b, int rank, float lora_scale,
+                                          void* stream) {
+    if (int rc = check_gemm_args(Xp, Wp, M, N, K)) return rc;
+    if (out_dtype != 0 && out_dtype != 1) return fail("out_dtype must be 0 (f32) or 1 (bf16)");
+    if (rank < 8 || rank > 64 || rank % 8 != 0) return fail("LoRA rank must be a multiple of 8 in [8, 64]");
+    if (M == 0 || N == 0) return 0;
+    if (!xscale || !wscale || !out || !lora_t || !lora_b) return fail("null pointer");
+    if (!aligned16(lora_t) || !aligned16(lora_b)) return fail("LoRA operands must be 16-byte aligned");
+    LoraArgs lora;
+    lora.t = lora_t;
+    lora.b = lora_b;
+    lora.rank = rank;
+    lora.scale = lora_scale;
+    const float* xs = static_cast<const float*>(xscale);
+    const float* ws = static_cast<const float*>(wscale);
+    const float* b = static_cast<const float*>(bias);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // 256 x 128 pair tiles leave TMEM room for the fp32 LoRA accumulator
+    if (out_dtype == 1) return launch_pair<128, false, kOutBF16, true>(Xp, Wp, xs, ws, b, out, M, N, K, s, lora);
+    return launch_pair<128, false, kOutF32, true>(Xp, Wp, xs, ws, b, out, M, N, K, s, lora);
 }
 
 CONVROT_API int ck_int4_convrot_gemm_splitk(const void* Xp, const void* Wp, const void* xscale,

@@ -47,7 +47,7 @@ constexpr int kSwizzle128 = 2;           // tcgen05 descriptor code for 128-byte
 constexpr int kEpiThreads = 128;         // four epilogue warps
 constexpr uint32_t kEpiBarrier = 1;      // named barrier id of the epilogue warps
 
-template <int BN, bool STAGED, bool SWAP>
+template <int BN, bool STAGED, bool SWAP, bool LORA = false>
 struct PairCfg {
     static constexpr int kBHalf = BN / 2;
     static constexpr int kABytes = 128 * kPairBKP;
@@ -58,21 +58,28 @@ struct PairCfg {
     // bf16 output tile staged for the TMA store: 128 rows x BN cols, 64-col boxes
     static constexpr int kStagingBytes = STAGED ? 128 * BN * 2 : 0;
     // 227 KB per block, minus alignment slack, barriers and the staging tile
-    static constexpr int kSmemForStages = 227 * 1024 - 2048 - 4 * BN * 4 - kStagingBytes;
+    // Dynamic-LoRA operands per tile: T rows (x A^T, bf16, 64 per 128 B row) and
+    // this CTA's half of the LoRA up-projection rows
+    static constexpr int kLoraTBytes = LORA ? 128 * 128 : 0;
+    static constexpr int kLoraBBytes = LORA ? kBHalf * 128 : 0;
+    static constexpr int kSmemForStages = 227 * 1024 - 2048 - 4 * BN * 4 - kStagingBytes - kLoraTBytes - kLoraBBytes;
     // TMA ring (shared memory) and expanded-A ring (TMEM slots) are sized
     // independently: the loads may run further ahead than TMEM allows.
-    static constexpr int kTmemStages0 = (static_cast<int>(kTmemCols) - BN) / kTmemStageCols;
+    static constexpr int kAccCols = LORA ? 2 * BN : BN;          // int32 accumulator (+ fp32 LoRA accumulator)
+    static constexpr int kTmemStages0 = (static_cast<int>(kTmemCols) - kAccCols) / kTmemStageCols;
     static constexpr int kStagesBySmem = kSmemForStages / kStageBytes;
     static constexpr int kStages = kStagesBySmem < 16 ? kStagesBySmem : 16;
     static constexpr int kTmemStages = kTmemStages0 < kStages ? kTmemStages0 : kStages;
     static constexpr int kStagingOffset = kStages * kStageBytes;
-    static constexpr int kBarOffset = kStagingOffset + kStagingBytes;
-    static constexpr int kNumBars = 4 * kStages + kTmemStages + 2;
+    static constexpr int kLoraOffset = kStagingOffset + kStagingBytes;
+    static constexpr int kBarOffset = kLoraOffset + kLoraTBytes + kLoraBBytes;
+    static constexpr int kNumBars = 4 * kStages + kTmemStages + 4;
     static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
     // per-tile column factors (scale, bias) x 2 tiles in flight
     static constexpr int kColOffset = kMiscOffset + 16;
     static constexpr int kSmemBytes = kColOffset + 2 * 2 * BN * 4 + 1024;
     static constexpr uint32_t kIdesc = idesc_i8(256, BN);
+    static constexpr uint32_t kIdescLora = idesc_bf16(256, BN);
     // swapped (weight-bound) tiles: three groups of four warps take turns on
     // whole stages (A and B), otherwise four A and four B expander warps
     static constexpr int kExpGroups = SWAP ? 3 : 1;
@@ -89,23 +96,24 @@ template <int OUT>
 __device__ __forceinline__ void store_row32(void* out, size_t obase, int n, int N, float (&v)[32],
                                             const float* bias_cols) {
     const bool full = (n + 32 <= N);
+    #define BIAS_AT(i) (bias_cols != nullptr ? bias_cols[i] : 0.0f)
     if constexpr (OUT == kOutBF16) {
         __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + obase;
         #pragma unroll
         for (int i = 0; i < 32; ++i)
-            if (full || n + i < N) o[i] = __float2bfloat16_rn(__fadd_rn(v[i], bias_cols[i]));
+            if (full || n + i < N) o[i] = __float2bfloat16_rn(__fadd_rn(v[i], BIAS_AT(i)));
     } else if constexpr (OUT == kOutF32) {
         float* o = reinterpret_cast<float*>(out) + obase;
         if (full && (N & 3) == 0) {
             #pragma unroll
             for (int i = 0; i < 32; i += 4)
                 *reinterpret_cast<float4*>(o + i) = make_float4(
-                    __fadd_rn(v[i], bias_cols[i]), __fadd_rn(v[i + 1], bias_cols[i + 1]),
-                    __fadd_rn(v[i + 2], bias_cols[i + 2]), __fadd_rn(v[i + 3], bias_cols[i + 3]));
+                    __fadd_rn(v[i], BIAS_AT(i)), __fadd_rn(v[i + 1], BIAS_AT(i + 1)),
+                    __fadd_rn(v[i + 2], BIAS_AT(i + 2)), __fadd_rn(v[i + 3], BIAS_AT(i + 3)));
         } else {
             #pragma unroll
             for (int i = 0; i < 32; ++i)
-                if (n + i < N) o[i] = __fadd_rn(v[i], bias_cols[i]);
+                if (n + i < N) o[i] = __fadd_rn(v[i], BIAS_AT(i));
         }
     } else if constexpr (OUT == kOutF32Accumulate) {
         float* o = reinterpret_cast<float*>(out) + obase;
@@ -113,18 +121,24 @@ __device__ __forceinline__ void store_row32(void* out, size_t obase, int n, int 
         for (int i = 0; i < 32; ++i)
             if (full || n + i < N) o[i] = __fadd_rn(o[i], v[i]);
     }
+    #undef BIAS_AT
 }
 
 // STAGED (bf16, not swapped, N % 8 == 0): output goes through a shared-memory
 // tile and TMA stores (tmap_out); otherwise the epilogue stores directly.
-template <int BN, bool SWAP, int OUT, bool STAGED>
+// LORA (not swapped): a rank <= 64 side path out += lora_scale * T[m, :] . B[n, :]
+// (T = x A^T precomputed, both bf16) on the tensor cores into a second, fp32
+// accumulator, added in the epilogue before the single output rounding.
+template <int BN, bool SWAP, int OUT, bool STAGED, bool LORA = false>
 __global__ void __launch_bounds__(kPairThreads, 1)
 int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_out,
+                      const __grid_constant__ CUtensorMap tmap_lt, const __grid_constant__ CUtensorMap tmap_lb,
                       const float* __restrict__ xscale, const float* __restrict__ wscale,
                       const float* __restrict__ bias, void* __restrict__ out, int M, int N, int K,
-                      int tiles_a, int num_tiles) {
-    using Cfg = PairCfg<BN, STAGED, SWAP>;
+                      int tiles_a, int num_tiles, float lora_scale) {
+    using Cfg = PairCfg<BN, STAGED, SWAP, LORA>;
+    static_assert(!LORA || !SWAP, "the LoRA side path is fused into non-swapped tiles");
     static_assert(!STAGED || (OUT == kOutBF16 && !SWAP), "staged epilogue is for bf16, non-swapped tiles");
     extern __shared__ __align__(1024) unsigned char psmem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -137,6 +151,10 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
     uint64_t* tmem_free_bar = bars + 4 * Cfg::kStages;           // [kTmemStages]
     uint64_t* acc_full_bar = tmem_free_bar + Cfg::kTmemStages;
     uint64_t* acc_empty_bar = acc_full_bar + 1;
+    uint64_t* lora_full_bar = acc_full_bar + 2;                  // even CTA: both CTAs' LoRA tiles landed
+    uint64_t* lora_empty_bar = acc_full_bar + 3;                 // LoRA MMAs of the previous tile done
+    unsigned char* lora_t = smem + Cfg::kLoraOffset;
+    unsigned char* lora_b = lora_t + Cfg::kLoraTBytes;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kMiscOffset);
     unsigned char* staging = smem + Cfg::kStagingOffset;
     float* col_factors = reinterpret_cast<float*>(smem + Cfg::kColOffset);   // [2][scale BN | bias BN]
@@ -162,10 +180,13 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         for (int t = 0; t < Cfg::kTmemStages; ++t) mbar_init(&tmem_free_bar[t], 1);
         mbar_init(acc_full_bar, 1);
         mbar_init(acc_empty_bar, 2);          // one epilogue arrival from each CTA
+        mbar_init(lora_full_bar, 1);
+        mbar_init(lora_empty_bar, 1);
         fence_mbar_init();
         tma_prefetch_desc(&tmap_a);
         tma_prefetch_desc(&tmap_b);
         if constexpr (STAGED) tma_prefetch_desc(&tmap_out);
+        if constexpr (LORA) { tma_prefetch_desc(&tmap_lt); tma_prefetch_desc(&tmap_lb); }
     }
     if (warp == 1) {
         tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -175,16 +196,27 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
     cluster_sync();                       // peer barriers initialised before any remote arrive
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const uint32_t tmem_a0 = tmem_base + BN;  // A stages follow the accumulator columns
+    const uint32_t tmem_a0 = tmem_base + Cfg::kAccCols;  // A stages follow the accumulator columns
+    const uint32_t tmem_lora = tmem_base + BN;           // fp32 LoRA accumulator (LORA only)
 
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer
             int it = 0;
             bool ok = true;
-            for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+            int lt = 0;
+            for (int t = cluster_id; t < num_tiles && ok; t += num_clusters, ++lt) {
                 const int a_row0 = (t % tiles_a) * 256 + static_cast<int>(cta) * 128;
                 const int b_row0 = (t / tiles_a) * BN + static_cast<int>(cta) * Cfg::kBHalf;
+                if constexpr (LORA) {
+                    if (!mbar_wait_bounded<true>(lora_empty_bar, (lt & 1) ^ 1)) {
+                        record_status(kStatusTimeoutProducer); ok = false; break;
+                    }
+                    const uint32_t lora_full_leader = mapa_shared(smem_u32(lora_full_bar), 0);
+                    if (cta == 0) mbar_arrive_expect_tx(lora_full_bar, 2 * (Cfg::kLoraTBytes + Cfg::kLoraBBytes));
+                    tma_load_2d_pair(lora_t, &tmap_lt, lora_full_leader, 0, a_row0);
+                    tma_load_2d_pair(lora_b, &tmap_lb, lora_full_leader, 0, b_row0);
+                }
                 for (int kt = 0; kt < num_kt; ++kt, ++it) {
                     const int s = it % Cfg::kStages;
                     const uint32_t ph = (it / Cfg::kStages) & 1;
@@ -227,6 +259,21 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                     }
                     mma_commit_pair_multicast(&empty_bar[s], 0x3);
                     mma_commit_pair_multicast(&tmem_free_bar[ts], 0x3);
+                }
+                if constexpr (LORA) {
+                    if (ok && !mbar_wait_bounded<true>(lora_full_bar, lt & 1)) {
+                        record_status(kStatusTimeoutMma); ok = false;
+                    }
+                    if (ok) {
+                        tc_fence_after();
+                        const uint32_t t_addr = smem_u32(lora_t), b_addr = smem_u32(lora_b);
+                        #pragma unroll
+                        for (int j = 0; j < 4; ++j)        // rank 64 = four K = 16 bf16 steps of a 128 B row
+                            mma_bf16_ss_pair(tmem_lora, smem_desc_kmajor(t_addr + 32 * j, 1024, kSwizzle128),
+                                             smem_desc_kmajor(b_addr + 32 * j, 1024, kSwizzle128),
+                                             Cfg::kIdescLora, j != 0);
+                        mma_commit_pair_multicast(lora_empty_bar, 0x3);
+                    }
                 }
                 if (ok) mma_commit_pair_multicast(acc_full_bar, 0x3);
             }
@@ -387,17 +434,23 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                 break;
             }
             tc_fence_after();
+            // two 32-column TMEM loads in flight per wait (int32 + fp32 chunk with LORA)
+            constexpr int kChunks = LORA ? 1 : 2;
             #pragma unroll 1
-            for (int cc = 0; cc < BN / 32; cc += 2) {
-                // two 32-column TMEM loads in flight per wait
-                uint32_t acc2[2][32];
+            for (int cc = 0; cc < BN / 32; cc += kChunks) {
+                uint32_t acc2[kChunks][32];
+                uint32_t lora2[kChunks][32];
                 __syncwarp();
                 const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + cc * 32;
                 tmem_ld_32x32b_x32(taddr, acc2[0]);
-                tmem_ld_32x32b_x32(taddr + 32, acc2[1]);
+                if constexpr (LORA) {
+                    tmem_ld_32x32b_x32(tmem_lora + (static_cast<uint32_t>(quarter * 32) << 16) + cc * 32, lora2[0]);
+                } else {
+                    tmem_ld_32x32b_x32(taddr + 32, acc2[kChunks - 1]);
+                }
                 tmem_ld_wait();
                 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
+                for (int h = 0; h < kChunks; ++h) {
                     uint32_t (&acc)[32] = acc2[h];
                     const int col0 = (cc + h) * 32;
                     const int b = b_tile0 + col0;                    // first B row of this chunk
@@ -434,6 +487,18 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                             const float d = static_cast<float>(static_cast<int32_t>(acc[i]) >> 8);
                             v[i] = __fmul_rn(__fmul_rn(d, lane_scale), cscale[col0 + i]);
                         }
+                        if constexpr (LORA) {
+                            // ((D xs) ws + bias) + scale * L: bias is added here, not at the store
+                            #pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                v[i] = __fadd_rn(__fadd_rn(v[i], cbias[col0 + i]),
+                                                 __fmul_rn(__uint_as_float(lora2[h][i]), lora_scale));
+                        }
+                        // with LORA the bias is already in v
+                        const float* vbias = LORA ? nullptr : cbias + col0;
+                        auto bias_of = [&](int i) -> float {
+                            if constexpr (LORA) return 0.0f; else return cbias[col0 + i];
+                        };
                         if constexpr (STAGED) {
                             // 32 bf16 = four 16-byte chunks of a 64-column, 128 B-swizzled box
                             unsigned char* box = staging + (col0 >> 6) * (128 * 128);
@@ -441,22 +506,21 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                             #pragma unroll
                             for (int q = 0; q < 4; ++q) {
                                 uint4 pk;
-                                const float* bq = cbias + col0 + 8 * q;
-                                __nv_bfloat162 p0 = __floats2bfloat162_rn(__fadd_rn(v[8 * q], bq[0]),
-                                                                          __fadd_rn(v[8 * q + 1], bq[1]));
-                                __nv_bfloat162 p1 = __floats2bfloat162_rn(__fadd_rn(v[8 * q + 2], bq[2]),
-                                                                          __fadd_rn(v[8 * q + 3], bq[3]));
-                                __nv_bfloat162 p2 = __floats2bfloat162_rn(__fadd_rn(v[8 * q + 4], bq[4]),
-                                                                          __fadd_rn(v[8 * q + 5], bq[5]));
-                                __nv_bfloat162 p3 = __floats2bfloat162_rn(__fadd_rn(v[8 * q + 6], bq[6]),
-                                                                          __fadd_rn(v[8 * q + 7], bq[7]));
+                                float w[8];
+                                #pragma unroll
+                                for (int e = 0; e < 8; ++e)
+                                    w[e] = LORA ? v[8 * q + e] : __fadd_rn(v[8 * q + e], bias_of(8 * q + e));
+                                __nv_bfloat162 p0 = __floats2bfloat162_rn(w[0], w[1]);
+                                __nv_bfloat162 p1 = __floats2bfloat162_rn(w[2], w[3]);
+                                __nv_bfloat162 p2 = __floats2bfloat162_rn(w[4], w[5]);
+                                __nv_bfloat162 p3 = __floats2bfloat162_rn(w[6], w[7]);
                                 memcpy(&pk.x, &p0, 4); memcpy(&pk.y, &p1, 4);
                                 memcpy(&pk.z, &p2, 4); memcpy(&pk.w, &p3, 4);
                                 *reinterpret_cast<uint4*>(box + r * 128 + (((c0 + q) ^ (r & 7)) << 4)) = pk;
                             }
                         } else {
                             if (!lane_ok) continue;
-                            store_row32<OUT>(out, static_cast<size_t>(a) * N + b, b, N, v, cbias + col0);
+                            store_row32<OUT>(out, static_cast<size_t>(a) * N + b, b, N, v, vbias);
                         }
                     }
                 }

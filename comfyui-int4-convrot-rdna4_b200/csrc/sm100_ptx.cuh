@@ -299,3 +299,43 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 }
 
 }  // namespace convrot
+
+namespace convrot {
+
+// Pair MMA, both operands from shared memory, bf16 inputs, fp32 accumulator.
+__device__ __forceinline__ void mma_bf16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Instruction descriptor for kind::f16 with bf16 A and B (K-major) and an fp32 accumulator.
+__host__ __device__ constexpr uint32_t idesc_bf16(uint32_t m, uint32_t n) {
+    return (1u << 4)            // D format: F32
+         | (1u << 7)            // A: bf16
+         | (1u << 10)           // B: bf16
+         | ((n >> 3) << 17)
+         | ((m >> 4) << 24);
+}
+
+}  // namespace convrot
+
+namespace convrot {
+
+// 2D tile load into this CTA's shared memory whose completion is signalled on
+// an mbarrier that may live in either CTA of the pair (`bar_cluster` is a
+// shared::cluster address, e.g. from mapa_shared).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* desc, uint32_t bar_cluster,
+                                                 int32_t x, int32_t y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];"
+        :: "r"(smem_u32(dst)), "l"(desc), "r"(bar_cluster), "r"(x), "r"(y)
+        : "memory");
+}
+
+}  // namespace convrot

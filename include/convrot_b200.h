@@ -52,6 +52,17 @@ int ck_int4_convrot_gemm(const void* Xp, const void* Wp, const void* xscale, con
                          const void* bias, void* out, int M, int N, int K, int out_dtype,
                          void* stream);
 
+/* ck_int4_convrot_gemm plus a fused Dynamic-LoRA side path:
+ *   out[m, n] = (((float(D) * xscale[m]) * wscale[n]) + bias[n]) + lora_scale * L[m, n],
+ *   L = lora_t[m, :] . lora_b[n, :]  (bf16 operands, fp32 tensor-core accumulation).
+ * lora_t = x A^T [M, rank] and lora_b = B [N, rank] are bf16 row-major; rank a
+ * multiple of 8 in [8, 64]. Replaces the unfused per-adapter `out + v.h(x, out)`
+ * of the node's forward (int4_ops.py:181-192, :383); no HIP export counterpart. */
+int ck_int4_convrot_gemm_lora(const void* Xp, const void* Wp, const void* xscale, const void* wscale,
+                              const void* bias, void* out, int M, int N, int K, int out_dtype,
+                              const void* lora_t, const void* lora_b, int rank, float lora_scale,
+                              void* stream);
+
 /* accum[m, n] += (float(D[m, n]) * xscale[m]) * wscale[n] into a caller-zeroed
  * f32 [M, N] buffer. Replaces ck_int4_convrot_gemm_splitk
  * (_int4/int4_gemm.hip:634-645). The reference splits K and adds float

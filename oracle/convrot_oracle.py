@@ -265,6 +265,25 @@ def int4_gemm_epilogue(acc: np.ndarray, xs: np.ndarray, ws: np.ndarray,
     raise ValueError(f"unknown out dtype {out_dtype!r}")
 
 
+def int4_gemm_epilogue_lora(acc, xs, ws, bias, lora_t, lora_b, scale: float,
+                            out_dtype: str = "bf16") -> np.ndarray:
+    """Epilogue with the Dynamic-LoRA side path:
+    (((float(D) * xs) * ws) + bias) + fp32(fp32(T . B^T) * scale), one output rounding.
+
+    T . B^T is formed in float64 and rounded once to fp32; the tensor cores
+    accumulate it in fp32 in an unspecified order, so the kernel may differ in
+    the last fp32 bits of that term (tests use a tolerance for this path).
+    """
+    v = acc.astype(np.float32) * np.asarray(xs, np.float32).reshape(-1, 1)
+    v = v * np.asarray(ws, np.float32).reshape(1, -1)
+    v = v + (np.asarray(bias, np.float32).reshape(1, -1) if bias is not None else np.float32(0.0))
+    lora = (np.asarray(lora_t, np.float64) @ np.asarray(lora_b, np.float64).T).astype(np.float32)
+    v = v + lora * np.float32(scale)
+    if out_dtype == "f32":
+        return v.astype(np.float32)
+    return f32_to_bf16_bits(v)
+
+
 def int4_convrot_gemm(xp, wp, xs, ws, bias, out_dtype: str = "bf16") -> np.ndarray:
     """Packed X [M,K/2] x packed W [N,K/2] -> dequantized output [M,N]."""
     return int4_gemm_epilogue(int4_gemm_acc(xp, wp), xs, ws, bias, out_dtype)

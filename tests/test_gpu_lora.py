@@ -1,0 +1,121 @@
+"""GPU tests of the Dynamic-LoRA side path fused into the int4 GEMM epilogue.
+
+The side path's arithmetic belongs to ComfyUI's LoRA adapter, which the
+reference does not vendor (int4_ops.py:181-192 calls ``v.h(x, out)``), so it has
+no pinned golden vectors; it is checked against the oracle's definition
+(oracle.int4_gemm_epilogue_lora) and against a plain fp32 torch reference.
+
+Tolerance: the tensor cores accumulate L = T . B^T in fp32 in an unspecified
+order, so the fused output may differ from the oracle by at most one unit in the
+last place of the output dtype, on a small fraction of elements.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import convrot_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ck():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import _int4
+    from _int4 import cuda_loader
+    assert _int4.is_available()
+    return cuda_loader
+
+
+def bits(t):
+    t = t.detach().cpu().contiguous()
+    return t.view(torch.int16).numpy().view(np.uint16) if t.dtype == torch.bfloat16 else t.numpy()
+
+
+def check_close_bf16(got_bits, ref_bits, summand_mag, max_frac=1e-3):
+    """One bf16 ulp of the result, plus fp32 accumulation noise of the summands
+    (sum of absolute products; matters only where the terms cancel)."""
+    g = orc.bf16_bits_to_f32(got_bits)
+    r = orc.bf16_bits_to_f32(ref_bits)
+    tol = np.maximum(np.abs(g), np.abs(r)) * np.float32(2.0 ** -7) + summand_mag * np.float32(2.0 ** -18)
+    assert np.all(np.abs(g - r) <= tol)
+    assert np.count_nonzero(got_bits != ref_bits) <= max(2, int(max_frac * g.size))
+
+
+@pytest.mark.parametrize("m,n,k,r", [(256, 256, 512, 64), (300, 1000, 1024, 16), (1024, 3072, 3072, 64),
+                                     (129, 264, 256, 8), (2048, 3072, 256, 32)])
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+def test_fused_lora_epilogue_vs_oracle(ck, m, n, k, r, out_dtype):
+    g = torch.Generator().manual_seed(m + n + r)
+    xp = torch.randint(-128, 128, (m, k // 2), generator=g, dtype=torch.int8).cuda()
+    wp = torch.randint(-128, 128, (n, k // 2), generator=g, dtype=torch.int8).cuda()
+    xs = (torch.rand(m, generator=g) * 0.05 + 1e-3).cuda()
+    ws = (torch.rand(n, generator=g) * 0.01 + 1e-4).cuda()
+    bias = (torch.randn(n, generator=g) * 0.01).cuda()
+    lt = (torch.randn(m, r, generator=g) * 0.5).to(torch.bfloat16).cuda()
+    lb = (torch.randn(n, r, generator=g) * 0.01).to(torch.bfloat16).cuda()
+    scale = 0.75
+    out = ck.int4_convrot_gemm_lora(xp, wp, xs, ws, bias, out_dtype, lt, lb, scale)
+    torch.cuda.synchronize()
+    acc = orc.int4_gemm_acc(bits(xp), bits(wp))
+    ref = orc.int4_gemm_epilogue_lora(acc, bits(xs), bits(ws), bits(bias), lt.float().cpu().numpy(),
+                                      lb.float().cpu().numpy(), scale,
+                                      "bf16" if out_dtype == torch.bfloat16 else "f32")
+    mag = (np.abs(acc.astype(np.float64) * bits(xs).reshape(-1, 1) * bits(ws).reshape(1, -1))
+           + np.abs(bits(bias)).reshape(1, -1)
+           + (np.abs(lt.float().cpu().numpy().astype(np.float64)) @ np.abs(lb.float().cpu().numpy()).T) * scale)
+    if out_dtype == torch.bfloat16:
+        check_close_bf16(bits(out), ref, mag)
+    else:
+        got = bits(out)
+        assert np.all(np.abs(got - ref) <= 2.0 ** -22 * np.abs(ref) + 2.0 ** -18 * mag)
+
+
+def test_fused_lora_zero_side_path_matches_plain_gemm(ck):
+    """With B = 0 the fused kernel must reproduce the plain GEMM bit for bit."""
+    m, n, k, r = 512, 1024, 1024, 64
+    g = torch.Generator().manual_seed(3)
+    xp = torch.randint(-128, 128, (m, k // 2), generator=g, dtype=torch.int8).cuda()
+    wp = torch.randint(-128, 128, (n, k // 2), generator=g, dtype=torch.int8).cuda()
+    xs = torch.rand(m, generator=g).cuda()
+    ws = torch.rand(n, generator=g).cuda() * 0.01
+    bias = torch.randn(n, generator=g).cuda() * 0.01
+    lt = torch.randn(m, r, generator=g).to(torch.bfloat16).cuda()
+    lb = torch.zeros(n, r, dtype=torch.bfloat16, device="cuda")
+    a = ck.int4_convrot_gemm_lora(xp, wp, xs, ws, bias, torch.bfloat16, lt, lb, 1.0)
+    b = ck.int4_convrot_gemm(xp, wp, xs, ws, bias, torch.bfloat16)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+def test_lora_api_single_and_stacked_adapters(ck):
+    import _int4
+    m, k, n = 384, 768, 512
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).cuda()
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.float16).cuda()
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.float16).cuda()
+    qw, ws = _int4.quantize_convrot_w4a4_weight(w, 256)
+    a1 = ((torch.randn(32, k, generator=g) * 0.01).cuda(), (torch.randn(n, 32, generator=g) * 0.01).cuda(), 2.0)
+    a2 = ((torch.randn(16, k, generator=g) * 0.01).cuda(), (torch.randn(n, 16, generator=g) * 0.01).cuda(), 0.5)
+    base = _int4.convrot_w4a4_linear(x, qw, ws, bias).float()
+    for adapters in ([a1], [a1, a2]):
+        out = _int4.convrot_w4a4_linear_lora(x, qw, ws, bias, adapters).float()
+        side = sum(s * ((x.float() @ d.float().t()) @ u.float().t()) for d, u, s in adapters)
+        ref = base + side
+        rel = (out - ref).norm() / ref.norm()
+        assert rel < 1e-2, rel
+        # the side path is actually present
+        assert (out - base).norm() / side.norm() > 0.9
+
+
+def test_lora_rejects_bad_rank(ck):
+    m, n, k = 64, 64, 64
+    xp = torch.zeros(m, k // 2, dtype=torch.int8, device="cuda")
+    wp = torch.zeros(n, k // 2, dtype=torch.int8, device="cuda")
+    s = torch.ones(max(m, n), device="cuda")
+    lt = torch.zeros(m, 72, dtype=torch.bfloat16, device="cuda")
+    lb = torch.zeros(n, 72, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(RuntimeError, match="rank"):
+        ck.int4_convrot_gemm_lora(xp, wp, s[:m], s[:n], None, torch.bfloat16, lt, lb, 1.0)
