@@ -44,19 +44,40 @@ M_TOKENS = 4608
 HIDDEN = 3072
 LAYERS = [("qkv", 3072, 9216), ("attn_out", 3072, 3072), ("mlp_up", 3072, 12288), ("mlp_down", 12288, 3072)]
 GROUP = 256
+LORA_RANK = 64
+
+# Per-config step: (name, M, K, N, lora_rank). Config 1 is the default (the
+# BASELINE metric's configuration); the others are the BASELINE parity configs.
+WORKLOADS = {
+    0: ("config0_single_linear", [("linear", 512, 3072, 3072, 0)]),
+    1: ("config1_flux_double_block_linears", [(name, M_TOKENS, k, n, 0) for name, k, n in LAYERS]),
+    3: ("config3_zimage_mlp_token_sweep", [(f"{nm}_m{m}", m, k, n, 0) for m in (1024, 4096, 16384)
+                                           for nm, k, n in (("mlp_up", 3840, 15360), ("mlp_down", 15360, 3840))]),
+    4: ("config4_dynamic_lora_m18432", [("mlp_up", 18432, 3072, 12288, LORA_RANK),
+                                        ("mlp_down", 18432, 12288, 3072, LORA_RANK)]),
+}
 METRIC = "w4a4_linear_tops"
 UNIT = "TOPS"
 L2_FLUSH_BYTES = 256 << 20
 
 
 def step_ops(m: int) -> int:
+    """Config-1 ops for m tokens (used by the CPU arm)."""
     return sum(2 * m * n * k for _, k, n in LAYERS)
 
 
-def workload_config(extra=None):
-    cfg = {"workload": "config1_flux_double_block_linears", "tokens_per_gpu": M_TOKENS, "hidden": HIDDEN,
-           "layers": {name: f"{k}->{n}" for name, k, n in LAYERS}, "convrot_groupsize": GROUP,
-           "l2": "flushed before every timed step (256 MiB write)"}
+def layer_ops(m, k, n, r) -> int:
+    """int4 GEMM ops, plus the LoRA side path's 2*M*r*(K+N) when present."""
+    return 2 * m * n * k + (2 * m * r * (k + n) if r else 0)
+
+
+def workload_config(cfg_id=1, extra=None):
+    name, layers = WORKLOADS[cfg_id]
+    cfg = {"workload": name,
+           "layers": {lname: f"M={m} {k}->{n}" + (f" +LoRA r={r}" if r else "") for lname, m, k, n, r in layers},
+           "convrot_groupsize": GROUP, "l2": "flushed before every timed step (256 MiB write)"}
+    if cfg_id == 1:
+        cfg.update({"tokens_per_gpu": M_TOKENS, "hidden": HIDDEN})
     if extra:
         cfg.update(extra)
     return cfg
@@ -204,7 +225,7 @@ def run_reference(args, rank):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3 * M_TOKENS / rows,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4",
         "data": "synthetic (seeded; config-1 shapes and value distributions)",
-        "config": workload_config({"cpu_rows_per_step": rows}),
+        "config": workload_config(1, {"cpu_rows_per_step": rows}),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -213,39 +234,82 @@ def run_reference(args, rank):
 
 # --------------------------------------------------------------------------- GPU arm
 
-def build_layers(device, seed):
+def build_layers(device, seed, cfg_id=1):
+    """Quantized layers and device-resident inputs of one step of config `cfg_id`."""
     import _int4
     gen = torch.Generator().manual_seed(seed)
     layers = []
-    for name, k, n in LAYERS:
+    xs = {}
+    for name, m, k, n, r in WORKLOADS[cfg_id][1]:
         w = (torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16).to(device)
         qw, ws = _int4.quantize_convrot_w4a4_weight(w.to(torch.float16), GROUP)
         bias = (torch.randn(n, generator=gen) * 0.01).to(torch.bfloat16).to(torch.float16).to(device)
-        layers.append({"name": name, "k": k, "n": n, "qw": qw, "ws": ws, "bias": bias,
-                       "bias32": bias.float().contiguous()})
+        layer = {"name": name, "m": m, "k": k, "n": n, "r": r, "qw": qw, "ws": ws, "bias": bias,
+                 "bias32": bias.float().contiguous()}
+        if r:
+            down = (torch.randn(r, k, generator=gen) * 0.01).to(torch.bfloat16).to(device)
+            up = (torch.randn(n, r, generator=gen) * 0.01).to(torch.bfloat16).to(device)
+            layer["adapters"] = [(down, up, 64.0 / r)]            # alpha = 64
+        layers.append(layer)
         del w
-    xs = {k: synth_activation(M_TOKENS, k, gen, device) for k in sorted({k for _, k, _ in LAYERS})}
+        if (m, k) not in xs:
+            xs[(m, k)] = synth_activation(m, k, gen, device)
     return layers, xs
 
 
 def device_step(layers, xs):
-    """One config-1 step through the public API on device-resident inputs."""
+    """One step through the public API on device-resident inputs."""
     import _int4
-    return [_int4.convrot_w4a4_linear(xs[l["k"]], l["qw"], l["ws"], l["bias"], GROUP) for l in layers]
+    outs = []
+    for l in layers:
+        x = xs[(l["m"], l["k"])]
+        if l["r"]:
+            outs.append(_int4.convrot_w4a4_linear_lora(x, l["qw"], l["ws"], l["bias"], l["adapters"], GROUP))
+        else:
+            outs.append(_int4.convrot_w4a4_linear(x, l["qw"], l["ws"], l["bias"], GROUP))
+    return outs
+
+
+def nsplit_step(layers, xs, rank, world):
+    """Config 4's 12288->3072 layer (with its LoRA side path unfused: the split
+    applies to the int4 product) column-split over the ranks: each rank owns N/P
+    weight rows, all ranks see the same M=18432 tokens, an NCCL all-gather
+    assembles [M, N]. Returns (step_fn, ops of the whole layer, layer list)."""
+    from _int4.nsplit import convrot_w4a4_linear_nsplit, shard_rows
+    down = next(l for l in layers if l["k"] == 12288)
+    q, w, b = shard_rows(down["qw"], down["ws"], down["bias"], rank, world)
+    ops = 2 * down["m"] * down["n"] * down["k"]
+    lay = [dict(down, n_out=down["n"])]
+
+    def step(inputs=None):
+        src = xs if inputs is None else inputs
+        return [convrot_w4a4_linear_nsplit(src[(down["m"], down["k"])], q, w, b, GROUP)]
+    return step, ops, lay
 
 
 def time_kernel(fn, iters, flush, stream):
-    """Average device time (ms) of fn() over `iters`, L2 flushed before each."""
+    """Average device time (ms) of the work fn() launches, L2 flushed before each run.
+
+    fn is captured once in a CUDA graph and replayed between two events on the
+    launching stream, so host-side launch work stays out of the measurement.
+    """
+    fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    torch.cuda.synchronize()
     total = 0.0
     for _ in range(iters):
         flush()
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        fn()
+        graph.replay()
         b.record(stream)
         b.synchronize()
         total += a.elapsed_time(b)
+    del graph
     return total / iters
 
 
@@ -261,11 +325,36 @@ def run_ours(args, rank, world, local_rank):
     def flush():
         flush_buf.fill_(1.0)
 
-    layers, xs = build_layers(device, seed=1234 + rank)
+    cfg_id = args.config
+    layers, xs = build_layers(device, seed=1234 + rank, cfg_id=cfg_id)
+    ops_per_step = sum(layer_ops(l["m"], l["k"], l["n"], l["r"]) for l in layers)
+    if args.nsplit:
+        step_fn, ops_per_step, layers = nsplit_step(layers, xs, rank, world)
+    else:
+        step_fn = lambda inputs=None: device_step(layers, xs if inputs is None else inputs)
     for _ in range(args.warmup):
         flush()
-        device_step(layers, xs)
+        step_fn()
     torch.cuda.synchronize()
+    if args.graph and not args.nsplit:
+        # Capture one step (the kernels of every layer) in a CUDA graph and
+        # replay it: per-launch host work (argument checks, tensor-map
+        # encoding) leaves the timed region, the device work is unchanged.
+        eager_fn = step_fn
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            graph_outs = eager_fn()
+        torch.cuda.synchronize()
+
+        def step_fn(inputs=None):
+            if inputs is not None:
+                return eager_fn(inputs)
+            graph.replay()
+            return graph_outs
+        for _ in range(2):
+            flush()
+            step_fn()
+        torch.cuda.synchronize()
 
     # ---------------- timed region: K steps, barrier + sync on both sides
     sampler = ClockSampler(local_rank)
@@ -279,7 +368,7 @@ def run_ours(args, rank, world, local_rank):
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        device_step(layers, xs)
+        step_fn()
         b.record(stream)
         events.append((a, b))
     torch.cuda.synchronize()
@@ -292,19 +381,20 @@ def run_ours(args, rank, world, local_rank):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         elapsed_ms = float(t.item())
     ms_per_step = elapsed_ms / args.steps
-    value = world * step_ops(M_TOKENS) / (ms_per_step * 1e-3) / 1e12
+    # weak scaling: every rank ran a full step; N-split: the ranks shared one step
+    value = (1 if args.nsplit else world) * ops_per_step / (ms_per_step * 1e-3) / 1e12
 
-    # ---------------- per-kernel roofline (dominant GEMM = MLP up), rank 0
+    # ---------------- per-kernel roofline (dominant GEMM = MLP up), rank 0, config 1
     extras = {}
-    if rank == 0:
+    if rank == 0 and cfg_id == 1 and not args.nsplit:
         peaks, peak_src = load_peaks()
         up = next(l for l in layers if l["name"] == "mlp_up")
-        xq, xsc = ck.convrot_quant_int4(xs[up["k"]], GROUP)
+        xq, xsc = ck.convrot_quant_int4(xs[(up["m"], up["k"])], GROUP)
         iters = 10
         gemm_ms = time_kernel(lambda: ck.int4_convrot_gemm(xq, up["qw"], xsc, up["ws"], up["bias32"],
                                                            torch.bfloat16), iters, flush, stream)
-        quant_ms = time_kernel(lambda: ck.convrot_quant_int4(xs[up["k"]], GROUP), iters, flush, stream)
-        m, k, n = M_TOKENS, up["k"], up["n"]
+        quant_ms = time_kernel(lambda: ck.convrot_quant_int4(xs[(up["m"], up["k"])], GROUP), iters, flush, stream)
+        m, k, n = up["m"], up["k"], up["n"]
         gemm_ops = 2 * m * n * k
         int8_peak = 2.0 * peaks["bf16_tflops"]           # dense int8 rate = 2x bf16 on B200
         achieved = gemm_ops / (gemm_ms * 1e-3) / 1e12
@@ -341,13 +431,14 @@ def run_ours(args, rank, world, local_rank):
 
     # ---------------- end to end: host buffers in, host buffers out, through the public API
     host_in = {k: v.cpu().pin_memory() for k, v in xs.items()}
-    host_out = [torch.empty((M_TOKENS, l["n"]), dtype=torch.bfloat16).pin_memory() for l in layers]
+    host_out = [torch.empty((l["m"], l["n_out"] if "n_out" in l else l["n"]), dtype=torch.bfloat16).pin_memory()
+                for l in layers]
     h2d = sum(v.numel() * v.element_size() for v in host_in.values())
     d2h = sum(v.numel() * v.element_size() for v in host_out)
 
     def e2e_step():
         dev_in = {k: v.to(device, non_blocking=True) for k, v in host_in.items()}
-        outs = device_step(layers, dev_in)
+        outs = step_fn(dev_in)
         for o, h in zip(outs, host_out):
             h.copy_(o, non_blocking=True)
 
@@ -370,17 +461,24 @@ def run_ours(args, rank, world, local_rank):
         t = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    e2e_value = world * step_ops(M_TOKENS) / (e2e_ms * 1e-3) / 1e12
+    e2e_value = (1 if args.nsplit else world) * ops_per_step / (e2e_ms * 1e-3) / 1e12
 
     if rank == 0:
-        cpu_tops, cpu_t, _ = cpu_sample(args.cpu_rows, args.cpu_seconds) if world == 1 else (None, None, None)
+        cpu_tops = None
+        if world == 1 and cfg_id == 1 and args.cpu_seconds > 0:
+            cpu_tops, _, _ = cpu_sample(args.cpu_rows, args.cpu_seconds)
+        par = (f"N-column split x{world} of the 12288->3072 layer, NCCL all-gather" if args.nsplit
+               else f"token-parallel replicas x{world}")
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "strong" if args.nsplit else "weak",
             "vs_baseline": None, "dtype": "int4",
             "data": "synthetic (seeded N(0,1) activations with 1% x20 outlier channels, N(0,0.02) weights)",
-            "config": workload_config({"parallelism": f"token-parallel replicas x{world}"}),
-            "gpu_launches": 2 * len(LAYERS) * args.steps,
+            "config": workload_config(cfg_id, {"parallelism": par,
+                                               "launch": "CUDA graph replay" if args.graph and not args.nsplit
+                                               else "eager launches"}),
+            "gpu_launches": 2 * len(layers) * args.steps,
             "clocks": clocks,
             "e2e": {"value": e2e_value, "unit": UNIT, "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
@@ -425,6 +523,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-rows", type=int, default=256, help="tokens per CPU-baseline sample")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline time budget")
+    ap.add_argument("--config", type=int, choices=sorted(WORKLOADS), default=1,
+                    help="BASELINE config whose linear set is one step (default 1, the metric's config)")
+    ap.add_argument("--nsplit", action="store_true",
+                    help="config 4's 12288->3072 layer split by output columns over the ranks (strong scaling)")
+    ap.add_argument("--no-graph", dest="graph", action="store_false",
+                    help="launch every kernel from the host each step instead of replaying a CUDA graph")
     ap.add_argument("--case", choices=["mlp_up", "small_m", "quant"], default=None,
                     help="run one kernel --iters times (profiling helper) instead of the benchmark")
     ap.add_argument("--iters", type=int, default=3)
@@ -434,6 +538,8 @@ def main():
         return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.nsplit:
+        args.config = 4
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
