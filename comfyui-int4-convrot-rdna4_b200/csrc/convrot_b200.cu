@@ -693,6 +693,217 @@ int4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_consta
 namespace convrot {
 
 // ===========================================================================
+// (3) Few-token GEMV on CUDA cores (M <= 4): weight streaming at HBM rate
+// ===========================================================================
+//
+// For a handful of tokens the product is bound by reading the packed weights
+// once. One block per SM owns a contiguous range of weight rows. A producer
+// lane streams them through a ring of shared-memory stages; a stage holds one
+// K slice of 2 * RW consecutive rows -- one bulk copy when a row is a single
+// slice (rows are contiguous), else one copy per row. RW (rows per warp) is 4,
+// 2 or 1 as rows get longer, so that a stage stays near 12-16 KB: the 2 * RW
+// rows of a stage belong to a pair of consumer warps, RW rows each, 32 / RW
+// lanes per row. A warp keeps its int32 accumulators across the slices of its
+// rows and reduces over each row's lanes with log2(32 / RW) shuffles.
+// Each warp pair owns its own ring slots, so the slot a pair waits on was last
+// filled for (and consumed by) that same pair: an mbarrier parity wait never
+// has to tell phase k - 1 from phase k + 1. Row groups go to the pairs round
+// robin and the producer fills slice j of every pair's group before slice
+// j + 1, which is the order the pairs consume them in. The producer starts
+// streaming before the activations are staged.
+// A packed word is split like in the tensor-core path -- (w & 0xF0F0F0F0) and
+// ((w << 4) & 0xF0F0F0F0) hold 16 * code as int8 -- and __dp4a of matching
+// halves accumulates 256 * sum(x * w) exactly in int32; the activation halves
+// are split once into shared memory. The epilogue is the GEMM's:
+// ((float(D) * xs[m]) * ws[n]) + bias[n], one rounding.
+
+constexpr int kGemvConsumers = 16;                         // consumer warps
+constexpr int kGemvThreads = (kGemvConsumers + 1) * 32;   // + one producer warp
+constexpr int kGemvIters = 16;                             // 16-byte steps per lane per slice
+// packed bytes of one row per stage with RW rows per warp (32 / RW lanes per row)
+__host__ __device__ constexpr int gemv_slice_max(int rw) { return kGemvIters * 16 * (32 / rw); }
+constexpr int kGemvMaxStages = 64;
+constexpr int kGemvBarrierBytes = 2 * kGemvMaxStages * 8;
+constexpr int kGemvSmemBytes = 227 * 1024;
+
+template <int MT, int RW, int OUT>
+__global__ void __launch_bounds__(kGemvThreads, 1)
+int4_gemv_kernel(const uint8_t* __restrict__ Xp, const uint8_t* __restrict__ Wp,
+                 const float* __restrict__ xscale, const float* __restrict__ wscale,
+                 const float* __restrict__ bias, void* __restrict__ out, int M, int N, int K,
+                 int slice, int nslices, int pairs, int slots_per_pair, int ring_off, int rows_per_block) {
+    constexpr int kLanes = 32 / RW;                           // lanes per row
+    constexpr int kStageRows = 2 * RW;                        // a stage feeds two warps
+    extern __shared__ __align__(128) unsigned char gv_smem[];
+    const int kb = K >> 1;                                    // packed bytes per row
+    const int chunks = kb >> 4;                               // 16-byte chunks per row
+    const int stage_bytes = kStageRows * slice;
+    const int stages = pairs * slots_per_pair;
+    uint64_t* full = reinterpret_cast<uint64_t*>(gv_smem);
+    uint64_t* empty = full + stages;
+    uint4* xs_sh = reinterpret_cast<uint4*>(gv_smem + kGemvBarrierBytes);   // [MT][high, low][chunks]
+    unsigned char* ring = gv_smem + ring_off;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row_begin = blockIdx.x * rows_per_block;
+    const int row_end = min(N, row_begin + rows_per_block);
+    const int groups = (row_end - row_begin + kStageRows - 1) / kStageRows;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 2);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == kGemvConsumers) {
+        if (lane == 0) {
+            // ---------------- producer: round r gives row group r * pairs + q to
+            // pair q; within a round, slice j of every group before slice j + 1
+            int k = 0;                                        // slot index within each pair's slots
+            uint32_t ph = 0;
+            for (int r0g = 0; r0g < groups; r0g += pairs) {
+                const int in_round = min(pairs, groups - r0g);
+                for (int j = 0; j < nslices; ++j) {
+                    const int off = j * slice;
+                    const int len = min(slice, kb - off);
+                    for (int q = 0; q < in_round; ++q) {
+                        const int s = q * slots_per_pair + k;
+                        if (!mbar_wait_bounded(&empty[s], ph ^ 1)) { record_status(kStatusTimeoutProducer); return; }
+                        const int r0 = row_begin + (r0g + q) * kStageRows;
+                        const int nr = min(kStageRows, row_end - r0);
+                        unsigned char* dst = ring + static_cast<size_t>(s) * stage_bytes;
+                        const uint8_t* src = Wp + static_cast<size_t>(r0) * kb + off;
+                        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nr * len));
+                        if (nslices == 1) {
+                            bulk_load(dst, src, static_cast<uint32_t>(nr * len), &full[s]);
+                        } else {
+                            for (int r = 0; r < nr; ++r)
+                                bulk_load(dst + r * slice, src + static_cast<size_t>(r) * kb,
+                                          static_cast<uint32_t>(len), &full[s]);
+                        }
+                    }
+                    if (++k == slots_per_pair) { k = 0; ph ^= 1u; }
+                }
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers
+    for (int i = threadIdx.x; i < MT * chunks; i += kGemvConsumers * 32) {
+        const int m = i / chunks, c = i - m * chunks;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (m < M) v = __ldg(reinterpret_cast<const uint4*>(Xp + static_cast<size_t>(m) * kb) + c);
+        xs_sh[(2 * m) * chunks + c] = make_uint4(v.x & 0xF0F0F0F0u, v.y & 0xF0F0F0F0u,
+                                                 v.z & 0xF0F0F0F0u, v.w & 0xF0F0F0F0u);
+        xs_sh[(2 * m + 1) * chunks + c] = make_uint4((v.x << 4) & 0xF0F0F0F0u, (v.y << 4) & 0xF0F0F0F0u,
+                                                     (v.z << 4) & 0xF0F0F0F0u, (v.w << 4) & 0xF0F0F0F0u);
+    }
+    named_barrier_sync(1, kGemvConsumers * 32);
+
+    // warp w takes rows [RW (w & 1), RW (w & 1) + RW) of row groups q, q + pairs, ... (q = w / 2)
+    const int q = warp >> 1;
+    if (q >= pairs) return;
+    const int kp = lane % kLanes;                             // lane within the row's lanes
+    const int row_in_stage = (warp & 1) * RW + lane / kLanes;
+    const float xsv = (OUT != kOutS32 && kp < MT && kp < M) ? xscale[kp] : 0.0f;
+    int k = 0;
+    uint32_t ph = 0;
+    for (int g = q; g < groups; g += pairs) {
+        const int n = row_begin + g * kStageRows + row_in_stage;
+        const bool live = n < row_end;
+        const bool writer = live && kp < MT && kp < M;        // lane kp writes token kp of its row
+        const size_t o = static_cast<size_t>(kp) * N + n;
+        // epilogue factors are requested before the stage waits, so their
+        // latency overlaps the weight copy
+        float wsv = 0.0f, addend = 0.0f;
+        if constexpr (OUT != kOutS32) {
+            if (live) {
+                wsv = wscale[n];
+                if constexpr (OUT == kOutF32Accumulate) {
+                    if (writer) addend = reinterpret_cast<const float*>(out)[o];
+                } else {
+                    if (bias != nullptr) addend = bias[n];
+                }
+            }
+        }
+        int acc4[MT][4];                                      // four independent dp4a chains per token
+        #pragma unroll
+        for (int m = 0; m < MT; ++m)
+            #pragma unroll
+            for (int e = 0; e < 4; ++e) acc4[m][e] = 0;
+        bool ok = true;
+        for (int j = 0, off = 0; j < nslices; ++j, off += slice) {
+            const int s = q * slots_per_pair + k;
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&full[s], ph))) {
+                if (lane == 0) record_status(kStatusTimeoutExpand);
+                ok = false;
+                break;
+            }
+            if (live) {
+                const int nc = min(slice, kb - off) >> 4;
+                const uint4* wrow = reinterpret_cast<const uint4*>(ring + static_cast<size_t>(s) * stage_bytes +
+                                                                   static_cast<size_t>(row_in_stage) * slice) + kp;
+                const uint4* xrow = xs_sh + (off >> 4) + kp;
+                #pragma unroll
+                for (int i = 0; i < kGemvIters; ++i) {
+                    if (kLanes * i < nc) {                    // uniform per row; ragged lanes read zero weights
+                        uint4 wv = make_uint4(0u, 0u, 0u, 0u);
+                        if (kp + kLanes * i < nc) wv = wrow[kLanes * i];
+                        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+                        int wh[4], wl[4];
+                        #pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            wh[e] = static_cast<int>(ww[e] & 0xF0F0F0F0u);
+                            wl[e] = static_cast<int>((ww[e] << 4) & 0xF0F0F0F0u);
+                        }
+                        #pragma unroll
+                        for (int m = 0; m < MT; ++m) {
+                            const uint4 xh = xrow[(2 * m) * chunks + kLanes * i];
+                            const uint4 xl = xrow[(2 * m + 1) * chunks + kLanes * i];
+                            const int xhw[4] = {static_cast<int>(xh.x), static_cast<int>(xh.y),
+                                                static_cast<int>(xh.z), static_cast<int>(xh.w)};
+                            const int xlw[4] = {static_cast<int>(xl.x), static_cast<int>(xl.y),
+                                                static_cast<int>(xl.z), static_cast<int>(xl.w)};
+                            #pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                acc4[m][e] = __dp4a(wh[e], xhw[e], acc4[m][e]);
+                                acc4[m][e] = __dp4a(wl[e], xlw[e], acc4[m][e]);
+                            }
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);            // this warp's rows of the slice are read
+            if (++k == slots_per_pair) { k = 0; ph ^= 1u; }
+        }
+        if (!ok) break;
+        int d = 0;
+        #pragma unroll
+        for (int m = 0; m < MT; ++m) {
+            int a = (acc4[m][0] + acc4[m][1]) + (acc4[m][2] + acc4[m][3]);
+            #pragma unroll
+            for (int sh = 1; sh < kLanes; sh <<= 1) a += __shfl_xor_sync(0xFFFFFFFFu, a, sh);
+            if (m == kp) d = a >> 8;
+        }
+        if (writer) {
+            if constexpr (OUT == kOutS32) {
+                reinterpret_cast<int32_t*>(out)[o] = d;
+            } else {
+                const float v = __fmul_rn(__fmul_rn(static_cast<float>(d), xsv), wsv);
+                const float y = __fadd_rn(addend, v);
+                if constexpr (OUT == kOutBF16) reinterpret_cast<__nv_bfloat16*>(out)[o] = __float2bfloat16_rn(y);
+                else reinterpret_cast<float*>(out)[o] = y;
+            }
+        }
+    }
+}
+
+// ===========================================================================
 // Host side
 // ===========================================================================
 
@@ -850,6 +1061,66 @@ int launch_pair(const void* Xp, const void* Wp, const float* xs, const float* ws
     return launch_pair_impl<BN, SWAP, OUT, false, LORA>(Xp, Wp, xs, ws, bias, out, M, N, K, lora, stream);
 }
 
+struct GemvPlan {
+    int rw, slice, nslices, pairs, slots_per_pair, ring_off;
+    size_t smem;
+    bool ok;
+};
+
+// Shared-memory plan of the few-token path for K: rows per warp by row length
+// (a stage of 2 * RW rows stays within 16 KB), split activation halves, then as
+// many ring stages as fit, shared out among up to eight consumer warp pairs
+// with at least two slots per pair.
+template <int MT>
+GemvPlan gemv_plan(int K) {
+    GemvPlan p{};
+    const int kb = K / 2;
+    p.rw = kb <= gemv_slice_max(4) ? 4 : kb <= gemv_slice_max(2) ? 2 : 1;
+    const int smax = gemv_slice_max(p.rw);
+    p.nslices = (kb + smax - 1) / smax;
+    p.slice = ((kb + p.nslices - 1) / p.nslices + 15) & ~15;
+    // 512 spare bytes after the activations: ragged lanes of the last step
+    // read up to 31 chunks past the end of a token's codes
+    p.ring_off = (kGemvBarrierBytes + MT * 2 * kb + 512 + 127) & ~127;
+    const int stage_bytes = 2 * p.rw * p.slice;
+    int stages = (kGemvSmemBytes - p.ring_off) / stage_bytes;
+    if (stages > kGemvMaxStages) stages = kGemvMaxStages;
+    // every consumer pair double-buffers at least: as many pairs as that allows
+    p.pairs = stages / 2 < kGemvConsumers / 2 ? stages / 2 : kGemvConsumers / 2;
+    p.slots_per_pair = p.pairs > 0 ? stages / p.pairs : 0;
+    p.ok = p.pairs >= 1;
+    p.smem = static_cast<size_t>(p.ring_off) + static_cast<size_t>(p.ok ? p.pairs * p.slots_per_pair : 0) * stage_bytes;
+    return p;
+}
+
+template <int MT, int RW, int OUT>
+int launch_gemv_rw(const void* Xp, const void* Wp, const float* xs, const float* ws, const float* bias,
+                   void* out, int M, int N, int K, const GemvPlan& p, cudaStream_t stream) {
+    auto kernel = int4_gemv_kernel<MT, RW, OUT>;
+    cudaError_t e = ensure_smem(kernel, static_cast<int>(p.smem));
+    if (e != cudaSuccess) return static_cast<int>(e);
+    // contiguous row ranges of equal length, one block per SM
+    int blocks = sm_count();
+    const int rows_per_block = (N + blocks - 1) / blocks;
+    blocks = (N + rows_per_block - 1) / rows_per_block;
+    kernel<<<blocks, kGemvThreads, p.smem, stream>>>(static_cast<const uint8_t*>(Xp), static_cast<const uint8_t*>(Wp),
+                                                     xs, ws, bias, out, M, N, K, p.slice, p.nslices, p.pairs,
+                                                     p.slots_per_pair, p.ring_off, rows_per_block);
+    return static_cast<int>(cudaGetLastError());
+}
+
+template <int MT, int OUT>
+int launch_gemv(const void* Xp, const void* Wp, const float* xs, const float* ws, const float* bias,
+                void* out, int M, int N, int K, cudaStream_t stream) {
+    const GemvPlan p = gemv_plan<MT>(K);
+    if (!p.ok) return fail("K too large for the few-token path");
+    if ((reinterpret_cast<uintptr_t>(Wp) & 15u) || (reinterpret_cast<uintptr_t>(Xp) & 15u))
+        return fail("packed operands must be 16-byte aligned");
+    if (p.rw == 4) return launch_gemv_rw<MT, 4, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, p, stream);
+    if (p.rw == 2) return launch_gemv_rw<MT, 2, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, p, stream);
+    return launch_gemv_rw<MT, 1, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, p, stream);
+}
+
 bool force_single_cta_kernel() {
     static const bool force = [] {
         const char* v = getenv("CONVROT_GEMM_SINGLE_CTA");
@@ -867,6 +1138,10 @@ int dispatch_gemm(const void* Xp, const void* Wp, const float* xs, const float* 
             return launch_gemm<256, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
         return launch_gemm<128, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
     }
+    // a few tokens: stream the weights on CUDA cores
+    if (M == 1 && gemv_plan<1>(K).ok) return launch_gemv<1, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
+    if (M <= 2 && gemv_plan<2>(K).ok) return launch_gemv<2, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
+    if (M <= 4 && gemv_plan<4>(K).ok) return launch_gemv<4, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
     if (M <= 32) return launch_pair<32, true, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
     if (M <= 64) return launch_pair<64, true, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
     if (M <= 128) return launch_pair<128, true, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);

@@ -113,12 +113,17 @@ def test_fused_quant_vs_reference_eager(ck, case):
 
 # ------------------------------------------------------------------ GEMM
 
-# Covers every kernel variant: swapped (weights in TMEM) for M <= 32/64/128, CTA
-# pairs above; partial k-stages (K/2 not a multiple of 64), tails in M and N,
-# a pair whose second CTA lies wholly outside the matrix.
+# Covers every kernel variant: the CUDA-core few-token path for M <= 4 (rows in
+# one K slice, in several slices, a shorter last slice, one row per block, and
+# K = 65536 where M = 3..4 falls back to the tensor path), swapped tiles (weights
+# in TMEM) for M <= 32/64/128, CTA pairs above; partial k-stages (K/2 not a
+# multiple of 64), tails in M and N, a pair whose second CTA lies wholly outside
+# the matrix.
 GEMM_SHAPES = [(1, 64, 64), (7, 100, 96), (128, 256, 3072), (129, 384, 512), (257, 3072, 3072),
                (64, 192, 32), (300, 1000, 1024), (512, 3072, 3072), (16, 128, 12288),
-               (33, 520, 160), (100, 300, 224), (65, 18432, 3072), (1, 18432, 3072), (4608, 256, 64)]
+               (33, 520, 160), (100, 300, 224), (65, 18432, 3072), (1, 18432, 3072), (4608, 256, 64),
+               (2, 1000, 3072), (3, 520, 160), (4, 2052, 12288), (1, 96, 32768),
+               (1, 3072, 12288), (3, 200, 7680), (2, 150, 65536), (4, 37, 3840)]
 
 
 @pytest.mark.parametrize("m,n,k", GEMM_SHAPES)
@@ -135,7 +140,8 @@ def test_gemm_int32_accumulators_exact(ck, m, n, k):
 # (2048, 3072): more output tiles than CTA pairs on the GPU (persistent tile loop);
 # (515, 2056): staged bf16 stores with tails in M and in the last 64-column box.
 @pytest.mark.parametrize("m,n,k", [(1, 64, 64), (77, 300, 1024), (256, 512, 3072), (200, 3072, 12288),
-                                   (2048, 3072, 256), (515, 2056, 320)])
+                                   (2048, 3072, 256), (515, 2056, 320), (3, 777, 3072), (4, 18432, 3072),
+                                   (1, 3072, 12288), (2, 300, 7680)])
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("with_bias", [True, False])
 def test_gemm_epilogue_bit_exact(ck, m, n, k, out_dtype, with_bias):
