@@ -18,6 +18,7 @@ from __future__ import annotations
 import torch
 
 from ._codec import _INT4_GROUP_SIZE
+from . import cuda_loader
 from .cuda_loader import convrot_quant_int4, int4_convrot_gemm, int4_convrot_gemm_lora
 from .cuda_loader import is_available as _lib_available
 from .eager import (
@@ -96,9 +97,8 @@ def convrot_w4a4_linear(
     _validate(x, qweight, convrot_groupsize, quant_group_size, linear_dtype)
     shape = x.shape
     x2d = x.reshape(-1, shape[-1]).contiguous()
-    qact, x_scale = convrot_quant_int4(x2d, convrot_groupsize)
     out_dtype = x.dtype if x.dtype in _NATIVE_OUT else torch.float32
-    out = int4_convrot_gemm(qact, qweight, x_scale, wscales, bias, out_dtype)
+    out = cuda_loader.convrot_w4a4_linear(x2d, qweight, wscales, bias, out_dtype, convrot_groupsize)
     if out.dtype != x.dtype:
         out = out.to(x.dtype)
     return out.reshape(*shape[:-1], qweight.shape[0])

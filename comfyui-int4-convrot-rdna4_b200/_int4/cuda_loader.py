@@ -28,7 +28,9 @@ _SIGNATURES = {
     "ck_int4_quant_rowwise": [_P, _I, _P, _P, _I, _I, _P],
     "ck_int4_convrot_gemm": [_P] * 6 + [_I] * 4 + [_P],
     "ck_int4_convrot_gemm_splitk": [_P] * 5 + [_I] * 4 + [_P],
-    "ck_int4_convrot_gemm_lora": [_P] * 6 + [_I] * 4 + [_P, _P, _I, ctypes.c_float, _P],
+    "ck_int4_convrot_gemm_lora": [_P] * 5 + [_I, _P] + [_I] * 4 + [_P, _P, _I, ctypes.c_float, _P],
+    "ck_convrot_w4a4_linear": [_P, _I, _P, _P, _P, _I, _P] + [_I] * 5 + [_P, ctypes.c_size_t, _P],
+    "ck_convrot_w4a4_linear_workspace_size": [_I, _I],
     "ck_int4_gemm_s32": [_P, _P, _P, _I, _I, _I, _P],
     "ck_convrot_device_status": [_P, ctypes.POINTER(ctypes.c_int)],
     "ck_convrot_last_error": [],
@@ -48,7 +50,8 @@ def _load():
             for name, argtypes in _SIGNATURES.items():
                 fn = getattr(lib, name)
                 fn.argtypes = argtypes
-                fn.restype = ctypes.c_char_p if name == "ck_convrot_last_error" else ctypes.c_int
+                fn.restype = {"ck_convrot_last_error": ctypes.c_char_p,
+                              "ck_convrot_w4a4_linear_workspace_size": ctypes.c_size_t}.get(name, ctypes.c_int)
             _lib = lib
     return _lib
 
@@ -160,15 +163,55 @@ def int4_convrot_gemm_lora(x_packed, w_packed, x_scale, w_scale, bias, out_dtype
     x_scale = x_scale.to(torch.float32).contiguous()
     w_scale = w_scale.to(torch.float32).contiguous()
     out = torch.empty((m, n), dtype=out_dtype, device=x_packed.device)
-    bias_ptr = 0
-    if bias is not None:
-        bias = bias.to(torch.float32).contiguous()
-        bias_ptr = bias.data_ptr()
+    bias, bias_ptr, bias_code = _bias_arg(bias)
     rc = lib.ck_int4_convrot_gemm_lora(x_packed.data_ptr(), w_packed.data_ptr(), x_scale.data_ptr(),
-                                       w_scale.data_ptr(), bias_ptr, out.data_ptr(), m, n, k,
+                                       w_scale.data_ptr(), bias_ptr, bias_code, out.data_ptr(), m, n, k,
                                        _OUT_DTYPE_CODE[out_dtype], lora_t.data_ptr(), lora_b.data_ptr(), r,
                                        float(lora_scale), _stream(x_packed))
     _check("ck_int4_convrot_gemm_lora", rc)
+    return out
+
+
+def _bias_arg(bias):
+    """(tensor kept alive, pointer, dtype code): f32/bf16/f16 bias is read as is by the kernels."""
+    if bias is None:
+        return None, 0, 0
+    if bias.dtype not in _IN_DTYPE_CODE:
+        bias = bias.to(torch.float32)
+    bias = bias.contiguous()
+    return bias, bias.data_ptr(), _IN_DTYPE_CODE[bias.dtype]
+
+
+def convrot_w4a4_linear(x, w_packed, w_scale, bias, out_dtype, convrot_groupsize: int = 256):
+    """x [M, K] @ W^T + bias through the fused entry ck_convrot_w4a4_linear.
+
+    Rotation + quantization into a workspace, then the int4 GEMM (a programmatic
+    dependent launch of the quantizer); the bias is read in its own dtype.
+    """
+    lib = _load()
+    if out_dtype not in _OUT_DTYPE_CODE:
+        raise ValueError(f"int4 gemm output dtype must be float32/bfloat16, got {out_dtype}")
+    if convrot_groupsize not in (16, 64, 256):
+        raise ValueError("fused convrot_quant_int4 supports groupsize 16/64/256")
+    _require_cuda(x, w_packed)
+    if x.dtype not in _IN_DTYPE_CODE:
+        raise ValueError(f"unsupported activation dtype {x.dtype}")
+    x = x.contiguous()
+    w_packed = w_packed.contiguous()
+    m, k = x.shape
+    n, kp = w_packed.shape
+    if kp * 2 != k:
+        raise ValueError(f"K mismatch: x {tuple(x.shape)} w {tuple(w_packed.shape)}")
+    w_scale = w_scale.to(torch.float32).contiguous()
+    bias, bias_ptr, bias_code = _bias_arg(bias)
+    out = torch.empty((m, n), dtype=out_dtype, device=x.device)
+    ws_bytes = lib.ck_convrot_w4a4_linear_workspace_size(m, k)
+    workspace = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=x.device)
+    rc = lib.ck_convrot_w4a4_linear(x.data_ptr(), _IN_DTYPE_CODE[x.dtype], w_packed.data_ptr(),
+                                    w_scale.data_ptr(), bias_ptr, bias_code, out.data_ptr(),
+                                    _OUT_DTYPE_CODE[out_dtype], m, n, k, convrot_groupsize,
+                                    workspace.data_ptr(), ws_bytes, _stream(x))
+    _check("ck_convrot_w4a4_linear", rc)
     return out
 
 

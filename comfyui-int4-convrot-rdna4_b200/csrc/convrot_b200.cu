@@ -1,6 +1,6 @@
 // ConvRot W4A4 linear path for NVIDIA B200 (sm_100a).
 //
-// Two kernels and the C-ABI that the Python host layer (ctypes) binds:
+// The kernels and the C-ABI that the Python host layer (ctypes) binds:
 //
 //  (1) convrot_quant_kernel: blockwise regular-Hadamard rotation of an
 //      activation row, row-wise absmax int4 quantization and nibble packing.
@@ -8,15 +8,17 @@
 //      (_int4/int4_gemm.hip:348-408), with the quantizer arithmetic of its
 //      eager path (_int4/eager.py:112-120) so codes and scales match eager.
 //
-//  (2) int4_gemm_kernel: packed-int4 x packed-int4 GEMM on the 5th-generation
-//      tensor cores. TMA brings packed [rows x 64 B] tiles into shared memory;
-//      expander warps split every byte into its high nibble (b & 0xF0) and its
-//      low nibble moved up (b << 4), both as int8 values 16*code; one thread
-//      issues tcgen05.mma.kind::i8 on the two halves into one int32 TMEM
-//      accumulator, which therefore holds 256 * sum_k x_k w_k exactly. The
-//      epilogue reads TMEM, shifts the accumulator back (exact), applies
+//  (2) int4_gemm_pair_kernel (gemm_pair.cuh): packed-int4 x packed-int4 GEMM
+//      on the 5th-generation tensor cores, CTA pairs (cta_group::2). Every
+//      packed byte is split into its high nibble (b & 0xF0) and its low nibble
+//      moved up (b << 4), both int8 values 16*code; tcgen05.mma.kind::i8 on the
+//      two halves accumulates 256 * sum_k x_k w_k exactly in int32 TMEM. The
+//      epilogue shifts the accumulator back (exact), applies
 //      ((D * xs[m]) * ws[n]) + bias[n] in fp32 (_int4/int4_gemm.hip:152-169)
 //      and stores bf16 or fp32.
+//
+//  (3) int4_gemv_kernel: the same product for M <= 4 on CUDA cores (__dp4a),
+//      streaming the weights through shared memory at HBM rate.
 //
 // The reference exports (_int4/int4_gemm.hip:627-741) are mirrored with the
 // same names, argument order and return codes: 0 on success, -1 when a shape
@@ -314,6 +316,8 @@ convrot_quant_kernel(const T* __restrict__ x, int8_t* __restrict__ qout, float* 
     }
     for (int r = tid; r < rows_per_block; r += kQuantThreads) rowmax[r] = 0u;
     __syncthreads();
+    griddep_wait();                   // x may be the previous kernel's output
+    griddep_launch_dependents();
     if (tid == 0) {
         if (blockIdx.x < groups) issue(blockIdx.x, 0);
         if (blockIdx.x + gridDim.x < groups) issue(blockIdx.x + gridDim.x, 1);
@@ -455,236 +459,22 @@ convrot_quant_kernel(const T* __restrict__ x, int8_t* __restrict__ qout, float* 
     }
 }
 
-// ===========================================================================
-// (2) int4 x int4 GEMM on tcgen05 (kind::i8, int32 accumulators in TMEM)
-// ===========================================================================
-
-constexpr int kBM = 128;                 // MMA M (accumulator lanes)
-constexpr int kBKP = 64;                 // packed bytes of K per stage (128 codes)
-constexpr int kSwizzle64 = 4;            // tcgen05 descriptor code for 64-byte swizzle
-constexpr int kExpWarps = 8;             // expander / epilogue warps
-constexpr int kGemmThreads = (4 + kExpWarps) * 32;
-
+// Output forms of the GEMM kernels: fp32, bf16, fp32 accumulate into `out`
+// (split-K export), raw int32 accumulators.
 enum : int { kOutF32 = 0, kOutBF16 = 1, kOutF32Accumulate = 2, kOutS32 = 3 };
 
-template <int BN>
-struct GemmCfg {
-    static constexpr int kStageBytes = 2 * (kBM + BN) * kBKP;        // packed/high + low halves
-    static constexpr int kStages = (BN == 256) ? 4 : 6;
-    static constexpr int kHalfBytes = (kBM + BN) * kBKP;               // one half (A then B)
-    static constexpr int kTxBytes = (kBM + BN) * kBKP;                 // TMA bytes per stage
-    static constexpr int kBarOffset = kStages * kStageBytes;
-    // barriers: full, expanded, empty per stage + accumulator-ready
-    static constexpr int kNumBars = 3 * kStages + 1;
-    static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
-    // tmem slot (16 B) + ws/bias tiles
-    static constexpr int kWsOffset = kMiscOffset + 16;
-    static constexpr int kBiasOffset = kWsOffset + BN * 4;
-    static constexpr int kSmemBytes = kBiasOffset + BN * 4 + 1024;    // + alignment slack
-    static constexpr uint32_t kIdesc = idesc_i8(kBM, BN);
+// Bias vector [N] in its own dtype (0 = f32, 1 = bf16, 2 = f16, the activation
+// codes of the C-ABI) or absent. Widening to fp32 is exact, so reading bf16/f16
+// here gives the same sums as adding a bias converted to fp32 beforehand.
+struct BiasRef {
+    const void* ptr;
+    int kind;
+    __device__ __forceinline__ float at(int n) const {
+        if (kind == 1) return __bfloat162float(static_cast<const __nv_bfloat16*>(ptr)[n]);
+        if (kind == 2) return __half2float(static_cast<const __half*>(ptr)[n]);
+        return static_cast<const float*>(ptr)[n];
+    }
 };
-
-template <int BN, int OUT>
-__global__ void __launch_bounds__(kGemmThreads, 1)
-int4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
-                 const float* __restrict__ xscale, const float* __restrict__ wscale,
-                 const float* __restrict__ bias, void* __restrict__ out, int M, int N, int K) {
-    using Cfg = GemmCfg<BN>;
-    extern __shared__ __align__(1024) unsigned char gsmem_raw[];
-    unsigned char* smem = reinterpret_cast<unsigned char*>(
-        (reinterpret_cast<uintptr_t>(gsmem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset);
-    uint64_t* full_bar = bars;
-    uint64_t* exp_bar = bars + Cfg::kStages;
-    uint64_t* empty_bar = bars + 2 * Cfg::kStages;
-    uint64_t* accum_bar = bars + 3 * Cfg::kStages;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kMiscOffset);
-    float* ws_tile = reinterpret_cast<float*>(smem + Cfg::kWsOffset);
-    float* bias_tile = reinterpret_cast<float*>(smem + Cfg::kBiasOffset);
-
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN;
-    const int m0 = blockIdx.y * kBM;
-    const int num_kt = ((K >> 1) + kBKP - 1) / kBKP;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < Cfg::kStages; ++s) {
-            mbar_init(&full_bar[s], 1);
-            mbar_init(&exp_bar[s], kExpWarps * 32);
-            mbar_init(&empty_bar[s], 1);
-        }
-        mbar_init(accum_bar, 1);
-        fence_mbar_init();
-        tma_prefetch_desc(&tmap_x);
-        tma_prefetch_desc(&tmap_w);
-    }
-    if (warp == 1) {
-        tmem_alloc(tmem_slot, BN);
-        tmem_relinquish();
-    }
-    if (warp >= 4 && OUT != kOutS32) {
-        for (int c = threadIdx.x - 128; c < BN; c += kExpWarps * 32) {
-            const int n = n0 + c;
-            ws_tile[c] = (n < N) ? wscale[n] : 0.0f;
-            bias_tile[c] = (bias != nullptr && n < N) ? bias[n] : 0.0f;
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem_base = *tmem_slot;
-
-    if (warp == 0) {
-        if (lane == 0) {
-            // ---------------- TMA producer
-            for (int kt = 0; kt < num_kt; ++kt) {
-                const int s = kt % Cfg::kStages;
-                const uint32_t ph = (kt / Cfg::kStages) & 1;
-                if (!mbar_wait_bounded(&empty_bar[s], ph ^ 1)) { record_status(kStatusTimeoutProducer); break; }
-                unsigned char* st = smem + s * Cfg::kStageBytes;
-                mbar_arrive_expect_tx(&full_bar[s], Cfg::kTxBytes);
-                tma_load_2d(st, &tmap_x, &full_bar[s], kt * kBKP, m0);
-                tma_load_2d(st + kBM * kBKP, &tmap_w, &full_bar[s], kt * kBKP, n0);
-            }
-        }
-    } else if (warp == 1) {
-        if (lane == 0) {
-            // ---------------- MMA issuer
-            for (int kt = 0; kt < num_kt; ++kt) {
-                const int s = kt % Cfg::kStages;
-                const uint32_t ph = (kt / Cfg::kStages) & 1;
-                if (!mbar_wait_bounded(&exp_bar[s], ph)) { record_status(kStatusTimeoutMma); break; }
-                tc_fence_after();
-                const uint32_t hi_base = smem_u32(smem + s * Cfg::kStageBytes);
-                const uint32_t lo_base = hi_base + Cfg::kHalfBytes;
-                #pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    const uint32_t a_base = half == 0 ? hi_base : lo_base;
-                    const uint32_t b_base = a_base + kBM * kBKP;
-                    #pragma unroll
-                    for (int ks = 0; ks < kBKP / 32; ++ks) {
-                        const uint64_t ad = smem_desc_kmajor(a_base + ks * 32, 8 * kBKP, kSwizzle64);
-                        const uint64_t bd = smem_desc_kmajor(b_base + ks * 32, 8 * kBKP, kSwizzle64);
-                        mma_i8_ss(tmem_base, ad, bd, Cfg::kIdesc, (kt | half | ks) != 0);
-                    }
-                }
-                mma_commit(&empty_bar[s]);
-            }
-            mma_commit(accum_bar);
-        }
-    } else if (warp >= 4) {
-        // ---------------- expanders: packed byte -> (b & 0xF0, b << 4), 16 B at a time
-        const int et = threadIdx.x - 128;
-        bool ok = true;
-        for (int kt = 0; kt < num_kt; ++kt) {
-            const int s = kt % Cfg::kStages;
-            const uint32_t ph = (kt / Cfg::kStages) & 1;
-            if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&full_bar[s], ph))) {
-                record_status(kStatusTimeoutExpand);
-                ok = false;
-                break;
-            }
-            uint4* hi = reinterpret_cast<uint4*>(smem + s * Cfg::kStageBytes);
-            uint4* lo = reinterpret_cast<uint4*>(smem + s * Cfg::kStageBytes + Cfg::kHalfBytes);
-            #pragma unroll 2
-            for (int c = et; c < Cfg::kHalfBytes / 16; c += kExpWarps * 32) {
-                const uint4 v = hi[c];
-                uint4 h, l;
-                h.x = v.x & 0xF0F0F0F0u; l.x = (v.x << 4) & 0xF0F0F0F0u;
-                h.y = v.y & 0xF0F0F0F0u; l.y = (v.y << 4) & 0xF0F0F0F0u;
-                h.z = v.z & 0xF0F0F0F0u; l.z = (v.z << 4) & 0xF0F0F0F0u;
-                h.w = v.w & 0xF0F0F0F0u; l.w = (v.w << 4) & 0xF0F0F0F0u;
-                hi[c] = h;
-                lo[c] = l;
-            }
-            fence_proxy_async_smem();
-            mbar_arrive(&exp_bar[s]);
-        }
-
-        // ---------------- epilogue: TMEM -> registers -> global
-        // Warp-uniform outcome: the TMEM loads below are warp-collective.
-        ok = __all_sync(0xFFFFFFFFu, ok && mbar_wait_bounded(accum_bar, 0));
-        if (!ok && lane == 0) record_status(kStatusTimeoutEpilogue);
-        tc_fence_after();
-        const int quarter = warp & 3;
-        const int col_half = (warp - 4) >> 2;
-        const int row = m0 + quarter * 32 + lane;
-        const float xs = (ok && row < M && OUT != kOutS32) ? xscale[row] : 0.0f;
-        #pragma unroll 1
-        for (int cc = 0; cc < BN / 64; ++cc) {
-            const int col0 = col_half * (BN / 2) + cc * 32;
-            uint32_t r[32];
-            __syncwarp();                                // tcgen05.ld is warp-collective
-            tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + col0, r);
-            tmem_ld_wait();
-            if (!ok || row >= M) continue;
-            const int n = n0 + col0;
-            const size_t obase = static_cast<size_t>(row) * N + n;
-            const bool full = (n + 32 <= N);
-            if constexpr (OUT == kOutS32) {
-                int32_t* o = reinterpret_cast<int32_t*>(out) + obase;
-                #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                    if (full || n + i < N) o[i] = static_cast<int32_t>(r[i]) >> 8;
-            } else {
-                float v[32];
-                #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const float d = static_cast<float>(static_cast<int32_t>(r[i]) >> 8);
-                    v[i] = __fmul_rn(__fmul_rn(d, xs), ws_tile[col0 + i]);
-                }
-                if constexpr (OUT == kOutBF16) {
-                    #pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = __fadd_rn(v[i], bias_tile[col0 + i]);
-                    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + obase;
-                    if (full && (N & 7) == 0) {
-                        #pragma unroll
-                        for (int i = 0; i < 32; i += 8) {
-                            uint4 pk;
-                            __nv_bfloat162 p0 = __floats2bfloat162_rn(v[i], v[i + 1]);
-                            __nv_bfloat162 p1 = __floats2bfloat162_rn(v[i + 2], v[i + 3]);
-                            __nv_bfloat162 p2 = __floats2bfloat162_rn(v[i + 4], v[i + 5]);
-                            __nv_bfloat162 p3 = __floats2bfloat162_rn(v[i + 6], v[i + 7]);
-                            memcpy(&pk.x, &p0, 4); memcpy(&pk.y, &p1, 4);
-                            memcpy(&pk.z, &p2, 4); memcpy(&pk.w, &p3, 4);
-                            *reinterpret_cast<uint4*>(o + i) = pk;
-                        }
-                    } else {
-                        #pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (n + i < N) o[i] = __float2bfloat16_rn(v[i]);
-                    }
-                } else if constexpr (OUT == kOutF32) {
-                    #pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = __fadd_rn(v[i], bias_tile[col0 + i]);
-                    float* o = reinterpret_cast<float*>(out) + obase;
-                    if (full && (N & 3) == 0) {
-                        #pragma unroll
-                        for (int i = 0; i < 32; i += 4)
-                            *reinterpret_cast<float4*>(o + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-                    } else {
-                        #pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (n + i < N) o[i] = v[i];
-                    }
-                } else {  // kOutF32Accumulate: out += ((D * xs) * ws), no bias
-                    float* o = reinterpret_cast<float*>(out) + obase;
-                    #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (full || n + i < N) o[i] = __fadd_rn(o[i], v[i]);
-                }
-            }
-        }
-    }
-
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc(tmem_base, BN);
-    }
-}
 
 }  // namespace convrot
 
@@ -730,7 +520,7 @@ template <int MT, int RW, int OUT>
 __global__ void __launch_bounds__(kGemvThreads, 1)
 int4_gemv_kernel(const uint8_t* __restrict__ Xp, const uint8_t* __restrict__ Wp,
                  const float* __restrict__ xscale, const float* __restrict__ wscale,
-                 const float* __restrict__ bias, void* __restrict__ out, int M, int N, int K,
+                 BiasRef bias, void* __restrict__ out, int M, int N, int K,
                  int slice, int nslices, int pairs, int slots_per_pair, int ring_off, int rows_per_block) {
     constexpr int kLanes = 32 / RW;                           // lanes per row
     constexpr int kStageRows = 2 * RW;                        // a stage feeds two warps
@@ -756,7 +546,16 @@ int4_gemv_kernel(const uint8_t* __restrict__ Xp, const uint8_t* __restrict__ Wp,
         }
         fence_mbar_init();
     }
+    if (warp == kGemvConsumers && lane == 0 && row_begin < row_end) {
+        // the block's first weight bytes into L2 while the previous kernel may
+        // still run (a hint: safe whatever it wrote)
+        const size_t span = static_cast<size_t>(row_end - row_begin) * kb;
+        const uint32_t bytes = static_cast<uint32_t>(min(span, static_cast<size_t>(stages) * stage_bytes));
+        bulk_prefetch_l2(Wp + static_cast<size_t>(row_begin) * kb, bytes);
+    }
     __syncthreads();
+    griddep_wait();                   // activations, scales and bias may be the previous kernel's output
+    griddep_launch_dependents();
 
     if (warp == kGemvConsumers) {
         if (lane == 0) {
@@ -826,7 +625,7 @@ int4_gemv_kernel(const uint8_t* __restrict__ Xp, const uint8_t* __restrict__ Wp,
                 if constexpr (OUT == kOutF32Accumulate) {
                     if (writer) addend = reinterpret_cast<const float*>(out)[o];
                 } else {
-                    if (bias != nullptr) addend = bias[n];
+                    if (bias.ptr != nullptr) addend = bias.at(n);
                 }
             }
         }
@@ -919,6 +718,25 @@ int sm_count() {
 }
 
 
+// Launch with programmatic stream serialization: the kernel may start its
+// prologue while the previous kernel in the stream drains; every kernel of this
+// library calls griddep_wait() before touching memory another kernel wrote.
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+}
+
 int fail(const char* msg) {
     snprintf(g_last_error, sizeof(g_last_error), "%s", msg);
     return -1;
@@ -937,9 +755,9 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
     return fn;
 }
 
-// Packed int4 matrix [rows, K/2] bytes, box [box_rows, box_bytes]; 64- or
-// 128-byte swizzle to match box_bytes.
-bool make_packed_tmap(CUtensorMap* map, const void* base, int rows, int K, int box_rows, int box_bytes = kBKP) {
+// Packed int4 matrix [rows, K/2] bytes, box [box_rows, 128 B], 128-byte swizzle.
+bool make_packed_tmap(CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
+    constexpr int box_bytes = kPairBKP;
     auto enc = get_encode_fn();
     if (!enc) return false;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K / 2), static_cast<cuuint64_t>(rows)};
@@ -948,28 +766,14 @@ bool make_packed_tmap(CUtensorMap* map, const void* base, int rows, int K, int b
     const cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
-                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
 template <typename KernelT>
 cudaError_t ensure_smem(KernelT kernel, int bytes) {
     return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-}
-
-template <int BN, int OUT>
-int launch_gemm(const void* Xp, const void* Wp, const float* xs, const float* ws, const float* bias,
-                void* out, int M, int N, int K, cudaStream_t stream) {
-    CUtensorMap tx, tw;
-    if (!make_packed_tmap(&tx, Xp, M, K, kBM) || !make_packed_tmap(&tw, Wp, N, K, BN))
-        return fail("cuTensorMapEncodeTiled failed (pointer not 16-byte aligned or driver entry point missing)");
-    auto kernel = int4_gemm_kernel<BN, OUT>;
-    cudaError_t e = ensure_smem(kernel, GemmCfg<BN>::kSmemBytes);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    dim3 grid((N + BN - 1) / BN, (M + kBM - 1) / kBM);
-    kernel<<<grid, kGemmThreads, GemmCfg<BN>::kSmemBytes, stream>>>(tx, tw, xs, ws, bias, out, M, N, K);
-    return static_cast<int>(cudaGetLastError());
 }
 
 // bf16 output [M, N] for TMA stores of 128-row x 64-column boxes (128 B swizzle).
@@ -1006,7 +810,7 @@ struct LoraArgs {
 };
 
 template <int BN, bool SWAP, int OUT, bool STAGED, bool LORA>
-int launch_pair_impl(const void* Xp, const void* Wp, const float* xs, const float* ws, const float* bias,
+int launch_pair_impl(const void* Xp, const void* Wp, const float* xs, const float* ws, BiasRef bias,
                      void* out, int M, int N, int K, const LoraArgs& lora, cudaStream_t stream) {
     using Cfg = PairCfg<BN, STAGED, SWAP, LORA>;
     const void* a_ptr = SWAP ? Wp : Xp;
@@ -1017,8 +821,8 @@ int launch_pair_impl(const void* Xp, const void* Wp, const float* xs, const floa
     memset(&to, 0, sizeof(to));
     memset(&tlt, 0, sizeof(tlt));
     memset(&tlb, 0, sizeof(tlb));
-    if (!make_packed_tmap(&ta, a_ptr, rows_a, K, 128, kPairBKP) ||
-        !make_packed_tmap(&tb, b_ptr, rows_b, K, BN / 2, kPairBKP))
+    if (!make_packed_tmap(&ta, a_ptr, rows_a, K, 128) ||
+        !make_packed_tmap(&tb, b_ptr, rows_b, K, BN / 2))
         return fail("cuTensorMapEncodeTiled failed (pointer not 16-byte aligned or driver entry point missing)");
     if (STAGED && !make_out_tmap(&to, out, M, N))
         return fail("cuTensorMapEncodeTiled failed for the output");
@@ -1038,13 +842,15 @@ int launch_pair_impl(const void* Xp, const void* Wp, const float* xs, const floa
     cfg.blockDim = dim3(kPairThreads, 1, 1);
     cfg.dynamicSmemBytes = Cfg::kSmemBytes;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, tlt, tlb, xs, ws, bias, out, M, N, K, tiles_a,
                            static_cast<int>(num_tiles), lora.scale);
     if (e != cudaSuccess) return static_cast<int>(e);
@@ -1052,7 +858,7 @@ int launch_pair_impl(const void* Xp, const void* Wp, const float* xs, const floa
 }
 
 template <int BN, bool SWAP, int OUT, bool LORA = false>
-int launch_pair(const void* Xp, const void* Wp, const float* xs, const float* ws, const float* bias,
+int launch_pair(const void* Xp, const void* Wp, const float* xs, const float* ws, BiasRef bias,
                 void* out, int M, int N, int K, cudaStream_t stream, const LoraArgs& lora = LoraArgs()) {
     if constexpr (OUT == kOutBF16 && !SWAP) {
         if ((N % 8) == 0 && aligned16(out))
@@ -1094,7 +900,7 @@ GemvPlan gemv_plan(int K) {
 }
 
 template <int MT, int RW, int OUT>
-int launch_gemv_rw(const void* Xp, const void* Wp, const float* xs, const float* ws, const float* bias,
+int launch_gemv_rw(const void* Xp, const void* Wp, const float* xs, const float* ws, BiasRef bias,
                    void* out, int M, int N, int K, const GemvPlan& p, cudaStream_t stream) {
     auto kernel = int4_gemv_kernel<MT, RW, OUT>;
     cudaError_t e = ensure_smem(kernel, static_cast<int>(p.smem));
@@ -1103,14 +909,14 @@ int launch_gemv_rw(const void* Xp, const void* Wp, const float* xs, const float*
     int blocks = sm_count();
     const int rows_per_block = (N + blocks - 1) / blocks;
     blocks = (N + rows_per_block - 1) / rows_per_block;
-    kernel<<<blocks, kGemvThreads, p.smem, stream>>>(static_cast<const uint8_t*>(Xp), static_cast<const uint8_t*>(Wp),
-                                                     xs, ws, bias, out, M, N, K, p.slice, p.nslices, p.pairs,
-                                                     p.slots_per_pair, p.ring_off, rows_per_block);
-    return static_cast<int>(cudaGetLastError());
+    e = launch_pdl(kernel, dim3(blocks), dim3(kGemvThreads), p.smem, stream, static_cast<const uint8_t*>(Xp),
+                   static_cast<const uint8_t*>(Wp), xs, ws, bias, out, M, N, K, p.slice, p.nslices, p.pairs,
+                   p.slots_per_pair, p.ring_off, rows_per_block);
+    return static_cast<int>(e);
 }
 
 template <int MT, int OUT>
-int launch_gemv(const void* Xp, const void* Wp, const float* xs, const float* ws, const float* bias,
+int launch_gemv(const void* Xp, const void* Wp, const float* xs, const float* ws, BiasRef bias,
                 void* out, int M, int N, int K, cudaStream_t stream) {
     const GemvPlan p = gemv_plan<MT>(K);
     if (!p.ok) return fail("K too large for the few-token path");
@@ -1121,23 +927,9 @@ int launch_gemv(const void* Xp, const void* Wp, const float* xs, const float* ws
     return launch_gemv_rw<MT, 1, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, p, stream);
 }
 
-bool force_single_cta_kernel() {
-    static const bool force = [] {
-        const char* v = getenv("CONVROT_GEMM_SINGLE_CTA");
-        return v != nullptr && v[0] == '1';
-    }();
-    return force;
-}
-
 template <int OUT>
-int dispatch_gemm(const void* Xp, const void* Wp, const float* xs, const float* ws, const float* bias,
+int dispatch_gemm(const void* Xp, const void* Wp, const float* xs, const float* ws, BiasRef bias,
                   void* out, int M, int N, int K, cudaStream_t stream) {
-    if (force_single_cta_kernel()) {
-        const long tiles256 = static_cast<long>((M + kBM - 1) / kBM) * ((N + 255) / 256);
-        if (N > 128 && tiles256 >= 148)
-            return launch_gemm<256, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
-        return launch_gemm<128, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
-    }
     // a few tokens: stream the weights on CUDA cores
     if (M == 1 && gemv_plan<1>(K).ok) return launch_gemv<1, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
     if (M <= 2 && gemv_plan<2>(K).ok) return launch_gemv<2, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
@@ -1183,9 +975,9 @@ int launch_quant_t(const void* x, void* q, void* s, int M, int K, cudaStream_t s
     const int groups = (M + rows - 1) / rows;
     const int resident = sm_count() * (per_sm > 0 ? per_sm : 1);
     const int grid = groups < resident ? groups : resident;
-    kernel<<<grid, kQuantThreads, bytes, stream>>>(static_cast<const T*>(x), static_cast<int8_t*>(q),
-                                                  static_cast<float*>(s), M, K, rows);
-    return static_cast<int>(cudaGetLastError());
+    e = launch_pdl(kernel, dim3(grid), dim3(kQuantThreads), bytes, stream, static_cast<const T*>(x),
+                   static_cast<int8_t*>(q), static_cast<float*>(s), M, K, rows);
+    return static_cast<int>(e);
 }
 
 template <int G>
@@ -1205,6 +997,28 @@ int check_quant_args(const void* x, int in_dtype, const void* q, const void* s, 
     if (M > 0 && (!x || !q || !s)) return fail("null pointer");
     if (!aligned16(x) || (reinterpret_cast<uintptr_t>(q) & 7u)) return fail("x must be 16-byte and qout 8-byte aligned");
     return 0;
+}
+
+// Workspace of the fused linear: packed activation codes [M, K/2], then the
+// row scales [M] f32, each from a 256-byte boundary.
+size_t linear_workspace_bytes(int M, int K) {
+    const size_t codes = (static_cast<size_t>(M) * static_cast<size_t>(K / 2) + 255) & ~static_cast<size_t>(255);
+    return codes + ((static_cast<size_t>(M) * 4 + 255) & ~static_cast<size_t>(255));
+}
+
+// Rotate + quantize x into the workspace, then the int4 GEMM (or GEMV) with the
+// bias read in its own dtype. The second launch is a programmatic dependent of
+// the first, so its prologue and weight prefetch overlap the quantizer.
+int run_linear(const void* x, int in_dtype, const void* Wp, const float* ws, BiasRef bias, void* out,
+               int out_dtype, int M, int N, int K, int G, unsigned char* workspace, cudaStream_t stream) {
+    void* q = workspace;
+    float* xs = reinterpret_cast<float*>(workspace + ((static_cast<size_t>(M) * (K / 2) + 255) & ~static_cast<size_t>(255)));
+    int rc = G == 256 ? launch_quant_g<256>(x, in_dtype, q, xs, M, K, stream)
+           : G == 64  ? launch_quant_g<64>(x, in_dtype, q, xs, M, K, stream)
+                      : launch_quant_g<16>(x, in_dtype, q, xs, M, K, stream);
+    if (rc != 0) return rc;
+    if (out_dtype == 1) return dispatch_gemm<kOutBF16>(q, Wp, xs, ws, bias, out, M, N, K, stream);
+    return dispatch_gemm<kOutF32>(q, Wp, xs, ws, bias, out, M, N, K, stream);
 }
 
 }  // namespace convrot
@@ -1245,18 +1059,44 @@ CONVROT_API int ck_int4_convrot_gemm(const void* Xp, const void* Wp, const void*
     if (!xscale || !wscale || !out) return fail("null scale or output pointer");
     const float* xs = static_cast<const float*>(xscale);
     const float* ws = static_cast<const float*>(wscale);
-    const float* b = static_cast<const float*>(bias);
+    const BiasRef b{bias, 0};
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (out_dtype == 1) return dispatch_gemm<kOutBF16>(Xp, Wp, xs, ws, b, out, M, N, K, s);
     return dispatch_gemm<kOutF32>(Xp, Wp, xs, ws, b, out, M, N, K, s);
 }
 
+CONVROT_API size_t ck_convrot_w4a4_linear_workspace_size(int M, int K) {
+    if (M <= 0 || K <= 0) return 0;
+    return linear_workspace_bytes(M, K);
+}
+
+CONVROT_API int ck_convrot_w4a4_linear(const void* x, int in_dtype, const void* Wp, const void* wscale,
+                                       const void* bias, int bias_dtype, void* out, int out_dtype,
+                                       int M, int N, int K, int G, void* workspace, size_t workspace_bytes,
+                                       void* stream) {
+    if (!(G == 16 || G == 64 || G == 256)) return fail("G must be 16, 64 or 256");
+    if (K <= 0 || K % G != 0) return fail("K must be divisible by G");
+    if (int rc = check_gemm_args(x, Wp, M, N, K)) return rc;
+    if (in_dtype < 0 || in_dtype > 2) return fail("in_dtype must be 0 (f32), 1 (bf16) or 2 (f16)");
+    if (out_dtype != 0 && out_dtype != 1) return fail("out_dtype must be 0 (f32) or 1 (bf16)");
+    if (bias_dtype < 0 || bias_dtype > 2) return fail("bias_dtype must be 0 (f32), 1 (bf16) or 2 (f16)");
+    if (M == 0 || N == 0) return 0;
+    if (!wscale || !out) return fail("null scale or output pointer");
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255u)) return fail("workspace must be 256-byte aligned");
+    if (workspace_bytes < linear_workspace_bytes(M, K))
+        return fail("workspace smaller than ck_convrot_w4a4_linear_workspace_size(M, K)");
+    return run_linear(x, in_dtype, Wp, static_cast<const float*>(wscale), BiasRef{bias, bias_dtype}, out,
+                      out_dtype, M, N, K, G, static_cast<unsigned char*>(workspace),
+                      static_cast<cudaStream_t>(stream));
+}
+
 CONVROT_API int ck_int4_convrot_gemm_lora(const void* Xp, const void* Wp, const void* xscale, const void* wscale,
-                                          const void* bias, void* out, int M, int N, int K, int out_dtype,
-                                          const void* lora_t, const void* lora_b, int rank, float lora_scale,
-                                          void* stream) {
+                                          const void* bias, int bias_dtype, void* out, int M, int N, int K,
+                                          int out_dtype, const void* lora_t, const void* lora_b, int rank,
+                                          float lora_scale, void* stream) {
     if (int rc = check_gemm_args(Xp, Wp, M, N, K)) return rc;
     if (out_dtype != 0 && out_dtype != 1) return fail("out_dtype must be 0 (f32) or 1 (bf16)");
+    if (bias_dtype < 0 || bias_dtype > 2) return fail("bias_dtype must be 0 (f32), 1 (bf16) or 2 (f16)");
     if (rank < 8 || rank > 64 || rank % 8 != 0) return fail("LoRA rank must be a multiple of 8 in [8, 64]");
     if (M == 0 || N == 0) return 0;
     if (!xscale || !wscale || !out || !lora_t || !lora_b) return fail("null pointer");
@@ -1268,7 +1108,7 @@ CONVROT_API int ck_int4_convrot_gemm_lora(const void* Xp, const void* Wp, const 
     lora.scale = lora_scale;
     const float* xs = static_cast<const float*>(xscale);
     const float* ws = static_cast<const float*>(wscale);
-    const float* b = static_cast<const float*>(bias);
+    const BiasRef b{bias, bias_dtype};
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // 256 x 128 pair tiles leave TMEM room for the fp32 LoRA accumulator
     if (out_dtype == 1) return launch_pair<128, false, kOutBF16, true>(Xp, Wp, xs, ws, b, out, M, N, K, s, lora);
@@ -1283,7 +1123,7 @@ CONVROT_API int ck_int4_convrot_gemm_splitk(const void* Xp, const void* Wp, cons
     if (M == 0 || N == 0) return 0;
     if (!xscale || !wscale || !accum) return fail("null scale or accumulator pointer");
     return dispatch_gemm<kOutF32Accumulate>(Xp, Wp, static_cast<const float*>(xscale),
-                                            static_cast<const float*>(wscale), nullptr, accum, M, N, K,
+                                            static_cast<const float*>(wscale), BiasRef{nullptr, 0}, accum, M, N, K,
                                             static_cast<cudaStream_t>(stream));
 }
 
@@ -1291,7 +1131,7 @@ CONVROT_API int ck_int4_gemm_s32(const void* Xp, const void* Wp, void* acc, int 
     if (int rc = check_gemm_args(Xp, Wp, M, N, K)) return rc;
     if (M == 0 || N == 0) return 0;
     if (!acc) return fail("null accumulator pointer");
-    return dispatch_gemm<kOutS32>(Xp, Wp, nullptr, nullptr, nullptr, acc, M, N, K,
+    return dispatch_gemm<kOutS32>(Xp, Wp, nullptr, nullptr, BiasRef{nullptr, 0}, acc, M, N, K,
                                   static_cast<cudaStream_t>(stream));
 }
 

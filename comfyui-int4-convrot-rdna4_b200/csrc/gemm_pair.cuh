@@ -135,7 +135,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                       const __grid_constant__ CUtensorMap tmap_out,
                       const __grid_constant__ CUtensorMap tmap_lt, const __grid_constant__ CUtensorMap tmap_lb,
                       const float* __restrict__ xscale, const float* __restrict__ wscale,
-                      const float* __restrict__ bias, void* __restrict__ out, int M, int N, int K,
+                      BiasRef bias, void* __restrict__ out, int M, int N, int K,
                       int tiles_a, int num_tiles, float lora_scale) {
     using Cfg = PairCfg<BN, STAGED, SWAP, LORA>;
     static_assert(!LORA || !SWAP, "the LoRA side path is fused into non-swapped tiles");
@@ -192,9 +192,24 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         tmem_alloc_pair(tmem_slot, kTmemCols);
         tmem_relinquish_pair();
     }
+    // The weight boxes of this CTA's first tile are pulled into L2 while the
+    // previous kernel may still be running (a hint: safe whatever it wrote).
+    if (warp == 0 && lane == 0 && cluster_id < num_tiles) {
+        const int t = cluster_id;
+        if constexpr (SWAP) {
+            const int w_row0 = (t % tiles_a) * 256 + static_cast<int>(cta) * 128;
+            for (int kt = 0; kt < num_kt; ++kt) tma_prefetch_l2_2d(&tmap_a, kt * kPairBKP, w_row0);
+        } else {
+            const int w_row0 = (t / tiles_a) * BN + static_cast<int>(cta) * Cfg::kBHalf;
+            for (int kt = 0; kt < num_kt; ++kt) tma_prefetch_l2_2d(&tmap_b, kt * kPairBKP, w_row0);
+        }
+    }
     tc_fence_before();
     cluster_sync();                       // peer barriers initialised before any remote arrive
     tc_fence_after();
+    // every operand, scale and output may belong to the previous kernel
+    griddep_wait();
+    griddep_launch_dependents();
     const uint32_t tmem_base = *tmem_slot;
     const uint32_t tmem_a0 = tmem_base + Cfg::kAccCols;  // A stages follow the accumulator columns
     const uint32_t tmem_lora = tmem_base + BN;           // fp32 LoRA accumulator (LORA only)
@@ -405,7 +420,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
             if (lane_ok && OUT != kOutS32) {
                 if constexpr (SWAP) {
                     lane_scale = wscale[a];
-                    lane_bias = bias != nullptr ? bias[a] : 0.0f;
+                    lane_bias = bias.ptr != nullptr ? bias.at(a) : 0.0f;
                 } else {
                     lane_scale = xscale[a];
                 }
@@ -420,7 +435,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                         cbias[c] = 0.0f;
                     } else {
                         cscale[c] = (n < N) ? wscale[n] : 0.0f;
-                        cbias[c] = (bias != nullptr && n < N) ? bias[n] : 0.0f;
+                        cbias[c] = (bias.ptr != nullptr && n < N) ? bias.at(n) : 0.0f;
                     }
                 }
             }

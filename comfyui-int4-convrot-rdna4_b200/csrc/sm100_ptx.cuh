@@ -339,3 +339,34 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* desc, ui
 }
 
 }  // namespace convrot
+
+namespace convrot {
+
+// ---------------------------------------------------------------- PDL, L2 prefetch
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialization may start while the previous kernel in the stream is still
+// draining; griddep_wait() blocks until that grid has completed and its memory
+// is visible (it returns at once for a normal launch). Nothing the previous
+// kernel may have written is read before it.
+__device__ __forceinline__ void griddep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Lets the next kernel in the stream (if launched with programmatic
+// serialization) start its own prologue.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Hint: pull `bytes` (multiple of 16, 16-byte aligned address) into L2.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(src), "r"(bytes) : "memory");
+}
+
+// Hint: pull one box of a tiled tensor map into L2 (x aligned like a load).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void* desc, int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
+                 :: "l"(desc), "r"(x), "r"(y) : "memory");
+}
+
+}  // namespace convrot

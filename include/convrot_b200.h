@@ -19,6 +19,8 @@
 #ifndef CONVROT_B200_H
 #define CONVROT_B200_H
 
+#include <stddef.h>
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -52,16 +54,41 @@ int ck_int4_convrot_gemm(const void* Xp, const void* Wp, const void* xscale, con
                          const void* bias, void* out, int M, int N, int K, int out_dtype,
                          void* stream);
 
+/* Workspace bytes that ck_convrot_w4a4_linear needs for M rows of K: the
+ * packed activation codes [M, K/2] and the row scales [M] f32, each from a
+ * 256-byte boundary. No reference counterpart (see below). */
+size_t ck_convrot_w4a4_linear_workspace_size(int M, int K);
+
+/* The whole W4A4 linear in one call: rotate + quantize x (as
+ * ck_convrot_quant_int4) into `workspace`, then
+ * out = ((float(D) * xs[m]) * wscale[n]) + bias[n] (as ck_int4_convrot_gemm).
+ * Replaces the two-call sequence of the reference's Python convrot_w4a4_linear
+ * (_int4/__init__.py:94-135: convrot_quant_int4 then int4_convrot_gemm); no
+ * single HIP export does both. Differences from calling the two exports:
+ *   - bias is read in its own dtype, bias_dtype 0 = f32, 1 = bf16, 2 = f16
+ *     (widening is exact, so results equal an fp32-converted bias);
+ *   - the GEMM launch is a programmatic dependent of the quantizer launch.
+ *   x [M, K] in_dtype (0 f32, 1 bf16, 2 f16); Wp [N, K/2]; wscale [N] f32;
+ *   out [M, N] out_dtype (0 f32, 1 bf16); G in {16, 64, 256}, K % G == 0,
+ *   K % 32 == 0; workspace 256-byte aligned, at least
+ *   ck_convrot_w4a4_linear_workspace_size(M, K) bytes, no initial contents
+ *   needed; two calls in flight at once need two workspaces. */
+int ck_convrot_w4a4_linear(const void* x, int in_dtype, const void* Wp, const void* wscale,
+                           const void* bias, int bias_dtype, void* out, int out_dtype,
+                           int M, int N, int K, int G, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
 /* ck_int4_convrot_gemm plus a fused Dynamic-LoRA side path:
  *   out[m, n] = (((float(D) * xscale[m]) * wscale[n]) + bias[n]) + lora_scale * L[m, n],
  *   L = lora_t[m, :] . lora_b[n, :]  (bf16 operands, fp32 tensor-core accumulation).
  * lora_t = x A^T [M, rank] and lora_b = B [N, rank] are bf16 row-major; rank a
- * multiple of 8 in [8, 64]. Replaces the unfused per-adapter `out + v.h(x, out)`
+ * multiple of 8 in [8, 64]; bias in bias_dtype as for ck_convrot_w4a4_linear.
+ * Replaces the unfused per-adapter `out + v.h(x, out)`
  * of the node's forward (int4_ops.py:181-192, :383); no HIP export counterpart. */
 int ck_int4_convrot_gemm_lora(const void* Xp, const void* Wp, const void* xscale, const void* wscale,
-                              const void* bias, void* out, int M, int N, int K, int out_dtype,
-                              const void* lora_t, const void* lora_b, int rank, float lora_scale,
-                              void* stream);
+                              const void* bias, int bias_dtype, void* out, int M, int N, int K,
+                              int out_dtype, const void* lora_t, const void* lora_b, int rank,
+                              float lora_scale, void* stream);
 
 /* accum[m, n] += (float(D[m, n]) * xscale[m]) * wscale[n] into a caller-zeroed
  * f32 [M, N] buffer. Replaces ck_int4_convrot_gemm_splitk

@@ -22,7 +22,7 @@ HEADER = os.path.join(ROOT, "include", "convrot_b200.h")
 def header_functions():
     text = open(HEADER).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return re.findall(r"\b(?:int|const char\*)\s+(ck_\w+)\s*\(", text)
+    return re.findall(r"\b(?:int|size_t|const char\*)\s+(ck_\w+)\s*\(", text)
 
 
 @pytest.fixture(scope="module")
@@ -82,6 +82,33 @@ def test_quant_rejects_bad_dtype_and_k(lib):
     assert lib.ck_convrot_quant_int4(16, 3, 16, 16, 4, 256, 256, None) == -1
     assert lib.ck_int4_quant_rowwise(16, 1, 16, 16, 4, 24, None) == -1
     assert lib.ck_convrot_quant_int4(16, 1, 16, 16, 0, 256, 256, None) == 0
+
+
+def test_linear_workspace_size(lib):
+    f = lib.ck_convrot_w4a4_linear_workspace_size
+    up = lambda v: (v + 255) // 256 * 256
+    for m, k in [(1, 64), (4608, 3072), (7, 12288), (18432, 12288)]:
+        assert f(m, k) == up(m * k // 2) + up(4 * m)
+    assert f(0, 3072) == 0
+
+
+def test_linear_rejects_bad_arguments(lib):
+    f = lib.ck_convrot_w4a4_linear
+    ws = lib.ck_convrot_w4a4_linear_workspace_size(4, 256)
+    ok = dict(x=256, ind=1, w=256, s=256, b=256, bd=1, out=256, od=1, m=4, n=8, k=256, g=256, wk=4096, wsz=ws)
+
+    def call(**kw):
+        a = {**ok, **kw}
+        return f(a["x"], a["ind"], a["w"], a["s"], a["b"], a["bd"], a["out"], a["od"], a["m"], a["n"], a["k"],
+                 a["g"], a["wk"], a["wsz"], None)
+    assert call(g=32) == -1
+    assert call(k=320) == -1                                  # not divisible by G
+    assert call(ind=3) == -1
+    assert call(od=2) == -1
+    assert call(bd=5) == -1
+    assert call(wk=4100) == -1 and b"256-byte" in lib.ck_convrot_last_error()
+    assert call(wsz=ws - 1) == -1 and b"workspace" in lib.ck_convrot_last_error()
+    assert call(m=0) == 0 and call(n=0) == 0                  # empty: nothing launched
 
 
 def test_python_api_validation_errors():

@@ -264,3 +264,58 @@ def test_linear_keeps_leading_dims_and_status_clear(ck):
     out = _int4.convrot_w4a4_linear(x, qw, ws)
     assert out.shape == (2, 3, 5, 96)
     assert ck.device_status() == 0
+
+
+# ------------------------------------------------------------------ fused linear entry
+
+# ck_convrot_w4a4_linear = ck_convrot_quant_int4 then ck_int4_convrot_gemm, with
+# the bias read in its own dtype: bit-identical to the two exports with an
+# fp32-converted bias, for the few-token path (M <= 4) and both tensor paths.
+@pytest.mark.parametrize("m,k,n", [(1, 3072, 3072), (3, 768, 520), (64, 1024, 384), (700, 3072, 1280)])
+@pytest.mark.parametrize("bias_dtype", [None, torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+def test_fused_linear_entry_matches_two_calls(ck, m, k, n, bias_dtype, out_dtype):
+    g = torch.Generator().manual_seed(m + n)
+    x = (torch.randn(m, k, generator=g) * 2).to(torch.bfloat16).cuda()
+    wq = torch.randint(-128, 128, (n, k // 2), generator=g, dtype=torch.int8).cuda()
+    ws = (torch.rand(n, generator=g) * 0.01 + 1e-4).cuda()
+    bias = None if bias_dtype is None else (torch.randn(n, generator=g) * 0.1).to(bias_dtype).cuda()
+    fused = ck.convrot_w4a4_linear(x, wq, ws, bias, out_dtype, 256)
+    q, xs = ck.convrot_quant_int4(x, 256)
+    two = ck.int4_convrot_gemm(q, wq, xs, ws, bias, out_dtype)
+    torch.cuda.synchronize()
+    assert torch.equal(fused, two)
+    assert ck.device_status() == 0
+
+
+def test_fused_linear_entry_back_to_back_in_a_graph(ck):
+    """Programmatic dependent launches chained through layers, captured in a
+    CUDA graph: each layer consumes the previous layer's output."""
+    import _int4
+    dims = [3072, 1536, 3072, 768]
+    g = torch.Generator().manual_seed(5)
+    layers = []
+    for a, b in zip(dims[:-1], dims[1:]):
+        w = (torch.randn(b, a, generator=g) * 0.02).to(torch.bfloat16).cuda()
+        qw, wsc = _int4.quantize_convrot_w4a4_weight(w, 256)
+        layers.append((qw, wsc, (torch.randn(b, generator=g) * 0.1).to(torch.bfloat16).cuda()))
+    x0 = torch.randn(300, dims[0], generator=g).to(torch.bfloat16).cuda()
+
+    def run(x):
+        for qw, wsc, b in layers:
+            x = _int4.convrot_w4a4_linear(x, qw, wsc, b)
+        return x
+    eager = run(x0)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = run(x0)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
+    # the same chain through the oracle
+    ref = to_storage(x0)
+    for qw, wsc, b in layers:
+        ref = orc.convrot_w4a4_linear(ref, to_storage(qw), to_storage(wsc), to_storage(b.float()), 256)
+    assert np.array_equal(to_storage(eager), ref)
