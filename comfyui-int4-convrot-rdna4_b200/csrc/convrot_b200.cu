@@ -36,6 +36,7 @@
 #include <mutex>
 
 #include "sm100_ptx.cuh"
+#include "linear_api.cuh"
 
 #define CONVROT_API extern "C" __attribute__((visibility("default")))
 
@@ -463,18 +464,6 @@ convrot_quant_kernel(const T* __restrict__ x, int8_t* __restrict__ qout, float* 
 // (split-K export), raw int32 accumulators.
 enum : int { kOutF32 = 0, kOutBF16 = 1, kOutF32Accumulate = 2, kOutS32 = 3 };
 
-// Bias vector [N] in its own dtype (0 = f32, 1 = bf16, 2 = f16, the activation
-// codes of the C-ABI) or absent. Widening to fp32 is exact, so reading bf16/f16
-// here gives the same sums as adding a bias converted to fp32 beforehand.
-struct BiasRef {
-    const void* ptr;
-    int kind;
-    __device__ __forceinline__ float at(int n) const {
-        if (kind == 1) return __bfloat162float(static_cast<const __nv_bfloat16*>(ptr)[n]);
-        if (kind == 2) return __half2float(static_cast<const __half*>(ptr)[n]);
-        return static_cast<const float*>(ptr)[n];
-    }
-};
 
 }  // namespace convrot
 
@@ -999,6 +988,18 @@ int check_quant_args(const void* x, int in_dtype, const void* q, const void* s, 
     return 0;
 }
 
+int check_linear_args(const void* x, int in_dtype, const void* Wp, const void* wscale, int bias_dtype,
+                      const void* out, int out_dtype, int M, int N, int K, int G) {
+    if (!(G == 16 || G == 64 || G == 256)) return fail("G must be 16, 64 or 256");
+    if (K <= 0 || K % G != 0) return fail("K must be divisible by G");
+    if (int rc = check_gemm_args(x, Wp, M, N, K)) return rc;
+    if (in_dtype < 0 || in_dtype > 2) return fail("in_dtype must be 0 (f32), 1 (bf16) or 2 (f16)");
+    if (out_dtype != 0 && out_dtype != 1) return fail("out_dtype must be 0 (f32) or 1 (bf16)");
+    if (bias_dtype < 0 || bias_dtype > 2) return fail("bias_dtype must be 0 (f32), 1 (bf16) or 2 (f16)");
+    if (M > 0 && N > 0 && (!wscale || !out)) return fail("null scale or output pointer");
+    return 0;
+}
+
 // Workspace of the fused linear: packed activation codes [M, K/2], then the
 // row scales [M] f32, each from a 256-byte boundary.
 size_t linear_workspace_bytes(int M, int K) {
@@ -1074,14 +1075,8 @@ CONVROT_API int ck_convrot_w4a4_linear(const void* x, int in_dtype, const void* 
                                        const void* bias, int bias_dtype, void* out, int out_dtype,
                                        int M, int N, int K, int G, void* workspace, size_t workspace_bytes,
                                        void* stream) {
-    if (!(G == 16 || G == 64 || G == 256)) return fail("G must be 16, 64 or 256");
-    if (K <= 0 || K % G != 0) return fail("K must be divisible by G");
-    if (int rc = check_gemm_args(x, Wp, M, N, K)) return rc;
-    if (in_dtype < 0 || in_dtype > 2) return fail("in_dtype must be 0 (f32), 1 (bf16) or 2 (f16)");
-    if (out_dtype != 0 && out_dtype != 1) return fail("out_dtype must be 0 (f32) or 1 (bf16)");
-    if (bias_dtype < 0 || bias_dtype > 2) return fail("bias_dtype must be 0 (f32), 1 (bf16) or 2 (f16)");
+    if (int rc = check_linear_args(x, in_dtype, Wp, wscale, bias_dtype, out, out_dtype, M, N, K, G)) return rc;
     if (M == 0 || N == 0) return 0;
-    if (!wscale || !out) return fail("null scale or output pointer");
     if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255u)) return fail("workspace must be 256-byte aligned");
     if (workspace_bytes < linear_workspace_bytes(M, K))
         return fail("workspace smaller than ck_convrot_w4a4_linear_workspace_size(M, K)");
