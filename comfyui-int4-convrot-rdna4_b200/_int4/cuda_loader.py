@@ -31,6 +31,7 @@ _SIGNATURES = {
     "ck_int4_convrot_gemm_lora": [_P] * 5 + [_I, _P] + [_I] * 4 + [_P, _P, _I, ctypes.c_float, _P],
     "ck_convrot_w4a4_linear": [_P, _I, _P, _P, _P, _I, _P] + [_I] * 5 + [_P, ctypes.c_size_t, _P],
     "ck_convrot_w4a4_linear_workspace_size": [_I, _I],
+    "ck_convrot_w4a4_linear_noalloc": [_P, _I, _P, _P, _P, _I, _P] + [_I] * 5 + [_P],
     "ck_int4_gemm_s32": [_P, _P, _P, _I, _I, _I, _P],
     "ck_convrot_device_status": [_P, ctypes.POINTER(ctypes.c_int)],
     "ck_convrot_last_error": [],
@@ -212,6 +213,30 @@ def convrot_w4a4_linear(x, w_packed, w_scale, bias, out_dtype, convrot_groupsize
                                     _OUT_DTYPE_CODE[out_dtype], m, n, k, convrot_groupsize,
                                     workspace.data_ptr(), ws_bytes, _stream(x))
     _check("ck_convrot_w4a4_linear", rc)
+    return out
+
+
+def convrot_w4a4_linear_noalloc(x, w_packed, w_scale, bias, out_dtype, convrot_groupsize: int = 256):
+    """As convrot_w4a4_linear, through ck_convrot_w4a4_linear_noalloc: the library
+    allocates nothing (its static per-device scratch holds the quantized
+    activations); only the output tensor is allocated here, by torch."""
+    lib = _load()
+    if out_dtype not in _OUT_DTYPE_CODE:
+        raise ValueError(f"int4 gemm output dtype must be float32/bfloat16, got {out_dtype}")
+    _require_cuda(x, w_packed)
+    if x.dtype not in _IN_DTYPE_CODE:
+        raise ValueError(f"unsupported activation dtype {x.dtype}")
+    x = x.contiguous()
+    w_packed = w_packed.contiguous()
+    m, k = x.shape
+    n = w_packed.shape[0]
+    w_scale = w_scale.to(torch.float32).contiguous()
+    bias, bias_ptr, bias_code = _bias_arg(bias)
+    out = torch.empty((m, n), dtype=out_dtype, device=x.device)
+    rc = lib.ck_convrot_w4a4_linear_noalloc(x.data_ptr(), _IN_DTYPE_CODE[x.dtype], w_packed.data_ptr(),
+                                            w_scale.data_ptr(), bias_ptr, bias_code, out.data_ptr(),
+                                            _OUT_DTYPE_CODE[out_dtype], m, n, k, convrot_groupsize, _stream(x))
+    _check("ck_convrot_w4a4_linear_noalloc", rc)
     return out
 
 

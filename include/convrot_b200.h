@@ -78,6 +78,24 @@ int ck_convrot_w4a4_linear(const void* x, int in_dtype, const void* Wp, const vo
                            int M, int N, int K, int G, void* workspace, size_t workspace_bytes,
                            void* stream);
 
+/* ck_convrot_w4a4_linear for callers that cannot allocate device memory: the
+ * same arguments minus the workspace, which is replaced by a static 128 MiB
+ * device array per device (placed when the library's no-alloc module loads;
+ * the entry itself allocates nothing). No reference counterpart: the
+ * reference always allocates its intermediates with torch.
+ *   - limit: ck_convrot_w4a4_linear_workspace_size(M, K) <= 134217728 bytes
+ *     (e.g. M = 18432 rows at K = 12288); larger sizes return -1 before any
+ *     CUDA call, with the reason in ck_convrot_last_error();
+ *   - nothing in the scratch has to start at zero (it is fully rewritten by
+ *     each call before it is read);
+ *   - one scratch per device: calls that may overlap in time (other streams,
+ *     other host threads) race on it; calls on one stream are ordered and safe;
+ *   - the first call on each device does the setup (a cudaGetSymbolAddress
+ *     with that device current): make it before capturing a CUDA graph. */
+int ck_convrot_w4a4_linear_noalloc(const void* x, int in_dtype, const void* Wp, const void* wscale,
+                                   const void* bias, int bias_dtype, void* out, int out_dtype,
+                                   int M, int N, int K, int G, void* stream);
+
 /* ck_int4_convrot_gemm plus a fused Dynamic-LoRA side path:
  *   out[m, n] = (((float(D) * xscale[m]) * wscale[n]) + bias[n]) + lora_scale * L[m, n],
  *   L = lora_t[m, :] . lora_b[n, :]  (bf16 operands, fp32 tensor-core accumulation).
