@@ -460,6 +460,224 @@ convrot_quant_kernel(const T* __restrict__ x, int8_t* __restrict__ qout, float* 
     }
 }
 
+// ---------------------------------------------------------------------------
+// (1b) bf16 rows, G in {64, 256}, K % 256 == 0: two threads per tile
+// ---------------------------------------------------------------------------
+//
+// A round is R whole rows (R * K/256 tiles, at most 192) brought into shared
+// memory by one bulk copy, double buffered two rounds ahead. Lane l of a warp
+// takes half h = l / 16 of tile t = l % 16 (of the warp's 16 tiles): rows
+// a = 8h .. 8h+7 of the 16 x 16 tile, i.e. a1 in {2h, 2h+1}, all a0 and b.
+// Its 128 values sit in fp32 pairs V[p][e] = {row with a1 = 2h, row with
+// a1 = 2h+1} at chunk p = (a0, bh) and column e of the chunk, so the H4 steps
+// along b0, b1 and a0 are paired-fp32 instructions in registers, and the step
+// along a1 exchanges the pairs with lane l ^ 16 (the tile's other half).
+// Shared-memory reads are conflict-free because lane t reads its chunk
+// c ^ (t & 7) into slot c: the XOR relabels digits b1 (by 2) and a0, and
+// H4 = J - 2R with S = (v0+v1)+(v2+v3) is unchanged under such a relabelling
+// (the sums only commute), so every slot ends up holding the rotated values of
+// the chunk it was loaded from; the stores undo the relabelling.
+// After rounding to bf16 (kept packed), the row absmax goes through shared
+// atomics (one per thread, three arrays so one barrier per round suffices).
+// Codes: t = bf16(y * fl(1/s)) as in the generic path, then bf16(t + 192) is
+// 192 + rint(t) exactly (unit spacing in [128, 256), ties to even), whose low
+// mantissa nibble is the two's-complement code.
+
+constexpr int kQ5MaxThreads = 384;
+constexpr int kQ5MaxTiles = kQ5MaxThreads / 2;           // tiles per round, at most
+constexpr int kQ5PairTiles = 96;                         // round size that lets two blocks share an SM
+constexpr int kQ5RowmaxOffset = 16;
+constexpr int kQ5SlabOffset = 2432;                      // 16 + 3 * 192 * 4, to 128 B
+// shared memory of a block of `threads` threads: two slabs of threads / 2 tiles
+constexpr int q5_smem_bytes(int threads) { return kQ5SlabOffset + 2 * (threads / 2) * 512; }
+
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+    __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+    uint32_t u;
+    memcpy(&u, &b, 4);
+    return u;
+}
+
+// max(|a|, |b|) per bf16 half, sign bits unspecified
+__device__ __forceinline__ uint32_t bf16x2_absmax(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_add(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+template <int G>
+__global__ void __launch_bounds__(kQ5MaxThreads, 1)
+convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restrict__ qout,
+                          float* __restrict__ scaleout, int M, int K, int rows_per_round) {
+    static_assert(G == 64 || G == 256, "two-digit tiles only");
+    extern __shared__ __align__(128) unsigned char q5smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(q5smem);
+    uint32_t* rowmax = reinterpret_cast<uint32_t*>(q5smem + kQ5RowmaxOffset);   // [3][kQ5MaxTiles]
+    unsigned char* slab = q5smem + kQ5SlabOffset;
+    const int slab_bytes = static_cast<int>(blockDim.x) * 256;   // blockDim / 2 tiles of 512 B
+
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int t = lane & 15, h = lane >> 4;
+    const int kx = t & 7;                              // chunk relabelling of this lane
+    const int tile = (tid >> 5) * 16 + t;              // tile of the round, in slab order
+    const int ntile = K >> 8;
+    const int my_row = tile / ntile;                   // row of the round
+    const int tile_in_row = tile - my_row * ntile;
+    const int rounds = (M + rows_per_round - 1) / rows_per_round;
+    const size_t round_elems = static_cast<size_t>(rows_per_round) * K;
+
+    auto issue = [&](int rd, int b) {
+        const int nr = min(rows_per_round, M - rd * rows_per_round);
+        const uint32_t bytes = static_cast<uint32_t>(static_cast<size_t>(nr) * K * 2);
+        mbar_arrive_expect_tx(&full[b], bytes);
+        bulk_load(slab + b * slab_bytes, x + static_cast<size_t>(rd) * round_elems, bytes, &full[b]);
+    };
+    if (tid == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        fence_mbar_init();
+    }
+    for (int i = tid; i < 3 * kQ5MaxTiles; i += blockDim.x) rowmax[i] = 0u;
+    __syncthreads();
+    griddep_wait();                                    // x may be the previous kernel's output
+    griddep_launch_dependents();
+    if (tid == 0) {
+        if (blockIdx.x < rounds) issue(blockIdx.x, 0);
+        if (blockIdx.x + gridDim.x < rounds) issue(blockIdx.x + gridDim.x, 1);
+    }
+
+    int it = 0;
+    for (int rd = blockIdx.x; rd < rounds; rd += gridDim.x, ++it) {
+        const int buf = it & 1;
+        const int row0 = rd * rows_per_round;
+        const int nrows = min(rows_per_round, M - row0);
+        const bool active = my_row < nrows;
+        uint32_t* rmax = rowmax + (it % 3) * kQ5MaxTiles;
+        const bool ok = mbar_wait_bounded(&full[buf], (it >> 1) & 1);
+
+        uint32_t packed[8][8];                         // rounded rotated values, bf16 pairs
+        // a tile's two halves are lanes l and l ^ 16: both in or both out
+        const unsigned mask = __ballot_sync(0xFFFFFFFFu, active && ok);
+        if (active && ok) {
+            const unsigned char* src = slab + buf * slab_bytes + tile * 512 + h * 256;
+            float2 V[8][8];
+            #pragma unroll
+            for (int s = 0; s < 16; ++s) {
+                const uint4 raw = *reinterpret_cast<const uint4*>(src + 16 * (s ^ kx));
+                const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float lo = __uint_as_float(w[i] << 16), hi = __uint_as_float(w[i] & 0xFFFF0000u);
+                    if (s < 8) { V[s][2 * i].x = lo; V[s][2 * i + 1].x = hi; }
+                    else       { V[s - 8][2 * i].y = lo; V[s - 8][2 * i + 1].y = hi; }
+                }
+            }
+            // along b0 (columns within a chunk)
+            #pragma unroll
+            for (int p = 0; p < 8; ++p) {
+                h4x2(V[p][0], V[p][1], V[p][2], V[p][3]);
+                h4x2(V[p][4], V[p][5], V[p][6], V[p][7]);
+            }
+            // along b1 = 2 bh + (e >> 2)
+            #pragma unroll
+            for (int p = 0; p < 8; p += 2)
+                #pragma unroll
+                for (int e = 0; e < 4; ++e) h4x2(V[p][e], V[p][e + 4], V[p + 1][e], V[p + 1][e + 4]);
+            // along a0 (p = 2 a0 + bh)
+            #pragma unroll
+            for (int bh = 0; bh < 2; ++bh)
+                #pragma unroll
+                for (int e = 0; e < 8; ++e) h4x2(V[bh][e], V[bh + 2][e], V[bh + 4][e], V[bh + 6][e]);
+            if constexpr (G == 256) {
+                // along a1, with the other half of the tile (lane ^ 16). Lane h
+                // holds {v_2h, v_2h+1}, receives the other pair r, and forms
+                // S = (v0+v1)+(v2+v3) (both lanes: sums commute) and its two
+                // outputs fma(-2, r.y, S), fma(-2, r.x, S).
+                #pragma unroll
+                for (int p = 0; p < 8; ++p) {
+                    #pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float2 v = V[p][e];
+                        const float ry = __shfl_xor_sync(mask, v.y, 16);
+                        const float rx = __shfl_xor_sync(mask, v.x, 16);
+                        const float s = __fadd_rn(__fadd_rn(v.x, v.y), __fadd_rn(rx, ry));
+                        float2 o = fma2(make_float2(-2.0f, -2.0f), make_float2(ry, rx), make_float2(s, s));
+                        o = mul2(o, make_float2(0.0625f, 0.0625f));
+                        packed[p][e] = bf16x2_bits(o.x, o.y);
+                    }
+                }
+            } else {
+                #pragma unroll
+                for (int p = 0; p < 8; ++p)
+                    #pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float2 o = mul2(V[p][e], make_float2(0.125f, 0.125f));
+                        packed[p][e] = bf16x2_bits(o.x, o.y);
+                    }
+            }
+            uint32_t m = 0u;
+            #pragma unroll
+            for (int p = 0; p < 8; ++p)
+                #pragma unroll
+                for (int e = 0; e < 8; ++e) m = bf16x2_absmax(m, packed[p][e]);
+            const uint32_t amax_bits = max((m & 0x7FFFu) << 16, m & 0x7FFF0000u);
+            atomicMax(&rmax[my_row], amax_bits);
+        }
+        if (__syncthreads_or(!ok)) { if (tid == 0) record_status(kStatusTimeoutExpand); break; }
+        // the slab buffer is consumed: refill it two rounds ahead; clear the
+        // row-max array of round it + 2 (last read before this barrier)
+        if (tid == 0 && rd + 2 * static_cast<int>(gridDim.x) < rounds) issue(rd + 2 * gridDim.x, buf);
+        for (int i = tid; i < rows_per_round; i += blockDim.x) rowmax[((it + 2) % 3) * kQ5MaxTiles + i] = 0u;
+
+        if (active) {
+            const float amax = fmaxf(__uint_as_float(rmax[my_row]), Act<__nv_bfloat16>::floor_value());
+            const float sc = Act<__nv_bfloat16>::round(__fdiv_rn(amax, 7.0f));
+            const float rcp = __frcp_rn(sc);
+            if (h == 0 && tile_in_row == 0) scaleout[row0 + my_row] = sc;
+            const float2 rcp2 = make_float2(rcp, rcp);
+            const uint32_t magic = 0x43404340u;            // bf16 pair {192, 192}
+            uint32_t words[8][2];                           // per chunk: {a1 = 2h row, a1 = 2h+1 row}
+            #pragma unroll
+            for (int p = 0; p < 8; ++p) {
+                uint32_t tb[4];
+                #pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                    uint32_t c[2];
+                    #pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const uint32_t y = packed[p][2 * jj + u];
+                        const float2 q = mul2(make_float2(__uint_as_float(y << 16), __uint_as_float(y & 0xFFFF0000u)), rcp2);
+                        c[u] = bf16x2_add(bf16x2_bits(q.x, q.y), magic) & 0x000F000Fu;
+                    }
+                    tb[jj] = c[0] | (c[1] << 4);                // byte 0: row 2h pair, byte 2: row 2h+1 pair
+                }
+                const uint32_t w01 = __byte_perm(tb[0], tb[1], 0x6240);
+                const uint32_t w23 = __byte_perm(tb[2], tb[3], 0x6240);
+                words[p][0] = __byte_perm(w01, w23, 0x5410);
+                words[p][1] = __byte_perm(w01, w23, 0x7632);
+            }
+            int8_t* dst = qout + static_cast<size_t>(row0 + my_row) * (K >> 1) + tile_in_row * 128 + h * 64;
+            const bool swap_b = kx & 1;                     // slot bh 0 holds columns 8..15
+            #pragma unroll
+            for (int a0s = 0; a0s < 4; ++a0s) {
+                const int a0n = a0s ^ (kx >> 1);
+                #pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const uint32_t w0 = words[2 * a0s][u], w1 = words[2 * a0s + 1][u];
+                    *reinterpret_cast<uint2*>(dst + (a0n + 4 * u) * 8) = swap_b ? make_uint2(w1, w0) : make_uint2(w0, w1);
+                }
+            }
+        }
+    }
+}
+
 // Output forms of the GEMM kernels: fp32, bf16, fp32 accumulate into `out`
 // (split-K export), raw int32 accumulators.
 enum : int { kOutF32 = 0, kOutBF16 = 1, kOutF32Accumulate = 2, kOutS32 = 3 };
@@ -969,8 +1187,37 @@ int launch_quant_t(const void* x, void* q, void* s, int M, int K, cudaStream_t s
     return static_cast<int>(e);
 }
 
+// bf16 rows of whole 256-column tiles, G in {64, 256}: the two-threads-per-tile kernel.
+template <int G>
+int launch_quant_bf16_tiles(const void* x, void* q, void* s, int M, int K, cudaStream_t stream) {
+    const int ntile = K / 256;
+    // Rounds of about 96 tiles let two blocks share an SM (their phases drift
+    // apart, which mixes the FMA-heavy rotation with the ALU-heavy packing);
+    // rows longer than that take one row per round.
+    const int blocks_per_sm = ntile <= kQ5PairTiles ? 2 : 1;
+    const int slots = blocks_per_sm * sm_count();
+    const int per_block = (M + slots - 1) / slots;
+    int rows = (ntile <= kQ5PairTiles ? kQ5PairTiles : kQ5MaxTiles) / ntile;
+    if (rows > per_block) rows = per_block;            // small M: spread the rows over the SMs
+    if (rows < 1) rows = 1;
+    const int tiles = (rows * ntile + 15) / 16 * 16;
+    const int smem = q5_smem_bytes(2 * tiles);
+    auto kernel = convrot_quant_bf16_kernel<G>;
+    cudaError_t e = ensure_smem(kernel, q5_smem_bytes(kQ5MaxThreads));
+    if (e != cudaSuccess) return static_cast<int>(e);
+    const int rounds = (M + rows - 1) / rows;
+    const int grid = rounds < slots ? rounds : slots;
+    e = launch_pdl(kernel, dim3(grid), dim3(2 * tiles), static_cast<size_t>(smem), stream,
+                   static_cast<const __nv_bfloat16*>(x), static_cast<int8_t*>(q), static_cast<float*>(s), M, K, rows);
+    return static_cast<int>(e);
+}
+
 template <int G>
 int launch_quant_g(const void* x, int in_dtype, void* q, void* s, int M, int K, cudaStream_t stream) {
+    if constexpr (G == 64 || G == 256) {
+        if (in_dtype == 1 && K % 256 == 0 && K / 256 <= kQ5MaxTiles)
+            return launch_quant_bf16_tiles<G>(x, q, s, M, K, stream);
+    }
     switch (in_dtype) {
         case 0: return launch_quant_t<float, G>(x, q, s, M, K, stream);
         case 1: return launch_quant_t<__nv_bfloat16, G>(x, q, s, M, K, stream);

@@ -59,8 +59,12 @@ def random_packed(rows, k, seed):
 
 # ------------------------------------------------------------------ quantizer
 
+# bf16 rows of whole 256-column tiles with G = 64/256 take the two-threads-per-tile
+# kernel (rounds of up to 192 tiles: 16 rows at K = 3072, 4 at 12288, 3 at 15360);
+# every other shape, dtype or G takes the half-warp-per-tile kernel.
 QUANT_SHAPES = [(1, 768, 256), (7, 3072, 256), (127, 512, 256), (128, 3840, 256), (129, 256, 256),
-                (33, 320, 64), (40, 576, 64), (17, 160, 16), (9, 48, 16), (3, 12288, 256), (2, 15360, 256)]
+                (33, 320, 64), (40, 576, 64), (17, 160, 16), (9, 48, 16), (3, 12288, 256), (2, 15360, 256),
+                (40, 768, 64), (300, 3072, 64), (5, 256, 64)]
 
 
 @pytest.mark.parametrize("m,k,g", QUANT_SHAPES)
@@ -82,6 +86,34 @@ def test_fused_quant_large_m(ck):
     qo, so = orc.convrot_quant_int4(to_storage(x[sl]), 256, "bf16")
     assert np.array_equal(to_storage(q[sl]), qo)
     assert np.array_equal(to_storage(s[sl]).view(np.uint32), so.view(np.uint32))
+
+
+@pytest.mark.parametrize("m,k", [(1000, 12288), (2000, 3072), (149, 15360)])
+def test_fused_quant_bf16_many_rounds_all_rows(ck, m, k):
+    """Several rounds per block, a partial last round, every row checked."""
+    x = activation(m, k, "bf16", seed=m)
+    q, s = ck.convrot_quant_int4(x, 256)
+    torch.cuda.synchronize()
+    qo, so = orc.convrot_quant_int4(to_storage(x), 256, "bf16")
+    assert np.array_equal(to_storage(s).view(np.uint32), so.view(np.uint32))
+    assert np.array_equal(to_storage(q), qo)
+
+
+@pytest.mark.parametrize("g", [64, 256])
+def test_fused_quant_zero_tiny_and_huge_rows(ck, g):
+    """All-zero rows (scale floor), subnormal-range rows and large (finite) values."""
+    x = activation(24, 3072, "bf16", seed=g).float()
+    x[3] = 0.0
+    x[7] = 1e-30
+    x[8, ::7] = -3e-39
+    x[11] *= 1e30
+    x[12, 5] = 1e35
+    x = x.to(torch.bfloat16)
+    q, s = ck.convrot_quant_int4(x, g)
+    torch.cuda.synchronize()
+    qo, so = orc.convrot_quant_int4(to_storage(x), g, "bf16")
+    assert np.array_equal(to_storage(s).view(np.uint32), so.view(np.uint32))
+    assert np.array_equal(to_storage(q), qo)
 
 
 @pytest.mark.parametrize("case", ["g256_bf16", "g64_bf16", "g16_bf16", "g256_f16", "g256_f32", "cfg0_bf16"])
