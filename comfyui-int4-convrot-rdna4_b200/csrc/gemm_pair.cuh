@@ -68,7 +68,14 @@ struct PairCfg {
     static constexpr int kAccCols = LORA ? 2 * BN : BN;          // int32 accumulator (+ fp32 LoRA accumulator)
     static constexpr int kTmemStages0 = (static_cast<int>(kTmemCols) - kAccCols) / kTmemStageCols;
     static constexpr int kStagesBySmem = kSmemForStages / kStageBytes;
-    static constexpr int kStages = kStagesBySmem < 16 ? kStagesBySmem : 16;
+    static constexpr int kStagesCapped = kStagesBySmem < 16 ? kStagesBySmem : 16;
+    // Swapped tiles: the three expander groups take TMA stages in turn, and TMA
+    // copies may land out of order, so each ring slot must always belong to
+    // the same group (which has then seen the slot's previous phase complete
+    // before waiting on the next: a parity wait cannot tell phase k - 1 from
+    // phase k + 1). The forwarders and the other waiters see stages complete
+    // in order, so they need no such rounding.
+    static constexpr int kStages = SWAP ? kStagesCapped - kStagesCapped % 3 : kStagesCapped;
     static constexpr int kTmemStages = kTmemStages0 < kStages ? kTmemStages0 : kStages;
     static constexpr int kStagingOffset = kStages * kStageBytes;
     static constexpr int kLoraOffset = kStagingOffset + kStagingBytes;
@@ -87,6 +94,7 @@ struct PairCfg {
     static constexpr int kReadyCount = kLocalArrivals + 1;         // + the odd CTA's forwarder
     static_assert(BN >= 32 && BN <= 256 && BN % 32 == 0, "pair MMA N must be a multiple of 32 in [32, 256]");
     static_assert(kStages >= 2 && kTmemStages >= 2, "pipeline needs at least two stages");
+    static_assert(!SWAP || (kExpGroups == 3 && kStages % 3 == 0), "swapped tiles: ring slots owned by one group");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
