@@ -400,7 +400,7 @@ def run_ours(args, rank, world, local_rank):
         achieved = gemm_ops / (gemm_ms * 1e-3) / 1e12
         traffic = load_traffic()
         extras["roofline"] = {
-            "kernel": "int4_gemm_kernel (MLP up 3072->12288, M=4608)",
+            "kernel": "int4_gemm_pair_kernel (MLP up 3072->12288, M=4608)",
             "bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
             "frac": achieved / int8_peak,
             "peak_source": f"2 x {peak_src} bf16 burst ({peaks['bf16_tflops']} TFLOP/s): B200 dense int8 rate",
@@ -410,7 +410,7 @@ def run_ours(args, rank, world, local_rank):
         }
         qbytes = 2 * m * k + m * k // 2 + 4 * m
         extras["quant_kernel"] = {
-            "kernel": "convrot_quant_kernel (K=3072, M=4608)", "bound": "hbm",
+            "kernel": "convrot_quant_bf16_kernel (K=3072, M=4608)", "bound": "hbm",
             "achieved": qbytes / (quant_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": qbytes / (quant_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "ms_per_launch": quant_ms,
         }
@@ -424,7 +424,7 @@ def run_ours(args, rank, world, local_rank):
                             iters, flush, stream)
         sm_bytes = 3072 // 2 + 18432 * 3072 // 2 + 4 + 4 * 18432 + 2 * 18432
         extras["small_m"] = {
-            "kernel": "int4_gemm_kernel (modulation 3072->18432, M=1)", "bound": "hbm",
+            "kernel": "int4_gemv_kernel (modulation 3072->18432, M=1)", "bound": "hbm",
             "achieved": sm_bytes / (sm_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": sm_bytes / (sm_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "ms_per_launch": sm_ms,
         }

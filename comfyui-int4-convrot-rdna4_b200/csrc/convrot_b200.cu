@@ -1068,7 +1068,12 @@ template <int BN, bool SWAP, int OUT, bool LORA = false>
 int launch_pair(const void* Xp, const void* Wp, const float* xs, const float* ws, BiasRef bias,
                 void* out, int M, int N, int K, cudaStream_t stream, const LoraArgs& lora = LoraArgs()) {
     if constexpr (OUT == kOutBF16 && !SWAP) {
-        if ((N % 8) == 0 && aligned16(out))
+        // The staged bf16 tile (64 KB at BN = 256) costs the k-stage ring one
+        // slot (3 instead of 4). Short rows drain a tile every few stages and
+        // gain more from TMA stores; long rows (24+ stages per tile) gain more
+        // from the deeper ring.
+        const bool long_rows = BN == 256 && K >= 6144;
+        if ((N % 8) == 0 && aligned16(out) && !long_rows)
             return launch_pair_impl<BN, SWAP, OUT, true, LORA>(Xp, Wp, xs, ws, bias, out, M, N, K, lora, stream);
     }
     return launch_pair_impl<BN, SWAP, OUT, false, LORA>(Xp, Wp, xs, ws, bias, out, M, N, K, lora, stream);

@@ -107,9 +107,23 @@ __device__ __forceinline__ void store_row32(void* out, size_t obase, int n, int 
     #define BIAS_AT(i) (bias_cols != nullptr ? bias_cols[i] : 0.0f)
     if constexpr (OUT == kOutBF16) {
         __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + obase;
-        #pragma unroll
-        for (int i = 0; i < 32; ++i)
-            if (full || n + i < N) o[i] = __float2bfloat16_rn(__fadd_rn(v[i], BIAS_AT(i)));
+        if (full && (reinterpret_cast<uintptr_t>(o) & 15u) == 0) {
+            #pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+                uint32_t w[4];
+                #pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    __nv_bfloat162 b2 = __floats2bfloat162_rn(__fadd_rn(v[i + 2 * e], BIAS_AT(i + 2 * e)),
+                                                              __fadd_rn(v[i + 2 * e + 1], BIAS_AT(i + 2 * e + 1)));
+                    memcpy(&w[e], &b2, 4);
+                }
+                *reinterpret_cast<uint4*>(o + i) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        } else {
+            #pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (full || n + i < N) o[i] = __float2bfloat16_rn(__fadd_rn(v[i], BIAS_AT(i)));
+        }
     } else if constexpr (OUT == kOutF32) {
         float* o = reinterpret_cast<float*>(out) + obase;
         if (full && (N & 3) == 0) {
