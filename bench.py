@@ -459,6 +459,7 @@ def run_ours(args, rank, world, local_rank):
             "achieved": qbytes / (quant_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": qbytes / (quant_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "ms_per_launch": quant_ms,
             "timing": "8 launches back to back over distinct 28 MB inputs in one CUDA graph, per launch",
+            "traffic": traffic.get("convrot_quant_bf16_kernel_bytes_per_launch") if traffic else None,
         }
         # small-M (weight-bound) layer: Flux modulation 3072 -> 18432 at M = 1
         wsm = (torch.randn(18432, 3072, device=device) * 0.02).to(torch.float16)
@@ -477,6 +478,7 @@ def run_ours(args, rank, world, local_rank):
             "achieved": sm_bytes / (sm_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": sm_bytes / (sm_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "ms_per_launch": sm_ms,
             "timing": "16 launches back to back over distinct 28 MB weight copies in one CUDA graph, per launch",
+            "traffic": traffic.get("int4_gemv_kernel_bytes_per_launch") if traffic else None,
         }
 
     # ---------------- end to end: host buffers in, host buffers out, through the public API
