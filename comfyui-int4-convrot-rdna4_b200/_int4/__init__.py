@@ -20,6 +20,7 @@ import torch
 from ._codec import _INT4_GROUP_SIZE
 from . import cuda_loader
 from .cuda_loader import convrot_quant_int4, int4_convrot_gemm, int4_convrot_gemm_lora
+from .cuda_loader import convrot_quant_int8, int8_convrot_gemm
 from .cuda_loader import is_available as _lib_available
 from .eager import (
     _build_hadamard,
@@ -28,7 +29,7 @@ from .eager import (
     quantize_convrot_w4a4_weight,
     quantize_signed_int4_rowwise,
 )
-from .int8_eager import convrot_w8a8_linear as _torch_convrot_w8a8_linear
+from .int8_eager import quantize_signed_int8_rowwise as _quantize_int8_rowwise
 
 __all__ = [
     "quantize_convrot_w4a4_weight",
@@ -163,9 +164,29 @@ def convrot_w8a8_linear(
     bias: torch.Tensor | None = None,
     convrot_groupsize: int = 256,
 ) -> torch.Tensor:
-    """``x @ W.T + bias`` for int8 ConvRot layers (qweight int8 [N, K], wscales [N]).
+    """``x @ W.T + bias`` for int8 ConvRot layers (qweight int8 [N, K], wscales [N]) -- the W8A8
+    middle tier (reference: _int4/__init__.py:141-175).
 
-    Computed with torch ops on the input's device (the int8 tier has no sm_100a
-    kernel yet).
+    bf16 rows of whole 256-column tiles (G = 64/256) are rotated and int8-quantized by
+    one kernel (ck_convrot_quant_int8); other activations take the torch rotation and
+    quantizer on the device, as the reference's layer does where its fused kernel does
+    not apply. The product always runs on the int8 tensor cores (ck_int8_convrot_gemm).
     """
-    return _torch_convrot_w8a8_linear(x, qweight, wscales, bias=bias, convrot_groupsize=convrot_groupsize)
+    if x.shape[-1] != qweight.shape[-1]:
+        raise ValueError(f"Input K={x.shape[-1]} does not match qweight K={qweight.shape[-1]}")
+    if x.shape[-1] % convrot_groupsize != 0:
+        raise ValueError(f"Input K={x.shape[-1]} not divisible by convrot_groupsize {convrot_groupsize}")
+    if not x.is_cuda:
+        raise ValueError("the B200 ConvRot kernels need CUDA tensors")
+    shape = x.shape
+    x2d = x.reshape(-1, shape[-1]).contiguous()
+    if cuda_loader.int8_quant_supported(x2d, convrot_groupsize):
+        qact, x_scale = cuda_loader.convrot_quant_int8(x2d, convrot_groupsize)
+    else:
+        h = _build_hadamard(convrot_groupsize, device=x2d.device, dtype=x2d.dtype)
+        qact, x_scale = _quantize_int8_rowwise(_rotate_activation(x2d, h, convrot_groupsize).contiguous())
+    out_dtype = x.dtype if x.dtype in _NATIVE_OUT else torch.float32
+    out = cuda_loader.int8_convrot_gemm(qact, qweight, x_scale, wscales, bias, out_dtype)
+    if out.dtype != x.dtype:
+        out = out.to(x.dtype)
+    return out.reshape(*shape[:-1], qweight.shape[0])

@@ -33,6 +33,9 @@ _SIGNATURES = {
     "ck_convrot_w4a4_linear_workspace_size": [_I, _I],
     "ck_convrot_w4a4_linear_noalloc": [_P, _I, _P, _P, _P, _I, _P] + [_I] * 5 + [_P],
     "ck_int4_gemm_s32": [_P, _P, _P, _I, _I, _I, _P],
+    "ck_convrot_quant_int8": [_P, _I, _P, _P, _I, _I, _I, _P],
+    "ck_int8_convrot_gemm": [_P] * 6 + [_I] * 4 + [_P],
+    "ck_int8_gemm_s32": [_P, _P, _P, _I, _I, _I, _P],
     "ck_convrot_device_status": [_P, ctypes.POINTER(ctypes.c_int)],
     "ck_convrot_last_error": [],
 }
@@ -281,3 +284,78 @@ def is_available() -> bool:
         return True
     except Exception:
         return False
+
+
+# --------------------------------------------------------------------- W8A8 tier
+
+
+def int8_quant_supported(x: torch.Tensor, convrot_groupsize: int) -> bool:
+    """Shapes the native int8 quantizer takes: bf16 rows of whole 256-column tiles, G = 64/256."""
+    k = x.shape[-1]
+    return (x.dtype == torch.bfloat16 and convrot_groupsize in (64, 256) and k % 256 == 0
+            and k // 256 <= 192)
+
+
+def convrot_quant_int8(x: torch.Tensor, convrot_groupsize: int):
+    """Fused rotation + row-wise int8 quantization: (int8 [M, K], scale f32 [M]).
+
+    Mirrors hip_loader.convrot_quant_int8 (_int4/hip_loader.py:95-113).
+    """
+    lib = _load()
+    if convrot_groupsize not in (16, 64, 256):
+        raise ValueError("fused convrot_quant_int8 supports groupsize 16/64/256")
+    _require_cuda(x)
+    if x.dtype not in _IN_DTYPE_CODE:
+        raise ValueError(f"unsupported activation dtype {x.dtype}")
+    x = x.contiguous()
+    m, k = x.shape
+    qout = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    scale = torch.empty((m,), dtype=torch.float32, device=x.device)
+    rc = lib.ck_convrot_quant_int8(x.data_ptr(), _IN_DTYPE_CODE[x.dtype], qout.data_ptr(),
+                                   scale.data_ptr(), m, k, convrot_groupsize, _stream(x))
+    _check("ck_convrot_quant_int8", rc)
+    return qout, scale
+
+
+def _int8_pair(x_int8: torch.Tensor, w_int8: torch.Tensor):
+    _require_cuda(x_int8, w_int8)
+    x_int8 = x_int8.contiguous()
+    w_int8 = w_int8.contiguous()
+    m, k = x_int8.shape
+    n, kw = w_int8.shape
+    if k != kw:
+        raise ValueError(f"K mismatch: x {tuple(x_int8.shape)} w {tuple(w_int8.shape)}")
+    return x_int8, w_int8, m, n, k
+
+
+def int8_convrot_gemm(x_int8, w_int8, x_scale, w_scale, bias, out_dtype):
+    """out[M,N] = (X @ W^T) * x_scale[:,None] * w_scale[None,:] (+ bias), int8 operands.
+
+    Mirrors hip_loader.int8_convrot_gemm (_int4/hip_loader.py:116-150).
+    """
+    lib = _load()
+    if out_dtype not in _OUT_DTYPE_CODE:
+        raise ValueError(f"int8 gemm output dtype must be float32/bfloat16, got {out_dtype}")
+    x_int8, w_int8, m, n, k = _int8_pair(x_int8, w_int8)
+    x_scale = x_scale.to(torch.float32).contiguous()
+    w_scale = w_scale.to(torch.float32).contiguous()
+    out = torch.empty((m, n), dtype=out_dtype, device=x_int8.device)
+    bias_ptr = 0
+    if bias is not None:
+        bias = bias.to(torch.float32).contiguous()
+        bias_ptr = bias.data_ptr()
+    rc = lib.ck_int8_convrot_gemm(x_int8.data_ptr(), w_int8.data_ptr(), x_scale.data_ptr(),
+                                  w_scale.data_ptr(), bias_ptr, out.data_ptr(), m, n, k,
+                                  _OUT_DTYPE_CODE[out_dtype], _stream(x_int8))
+    _check("ck_int8_convrot_gemm", rc)
+    return out
+
+
+def int8_gemm_s32(x_int8, w_int8):
+    """Exact int32 accumulators [M, N] of the int8 product."""
+    lib = _load()
+    x_int8, w_int8, m, n, k = _int8_pair(x_int8, w_int8)
+    acc = torch.empty((m, n), dtype=torch.int32, device=x_int8.device)
+    rc = lib.ck_int8_gemm_s32(x_int8.data_ptr(), w_int8.data_ptr(), acc.data_ptr(), m, n, k, _stream(x_int8))
+    _check("ck_int8_gemm_s32", rc)
+    return acc

@@ -511,11 +511,14 @@ __device__ __forceinline__ uint32_t bf16x2_add(uint32_t a, uint32_t b) {
     return d;
 }
 
-template <int G>
+// BITS = 4: packed int4 codes [M, K/2] (scale = absmax / 7); BITS = 8: int8 codes
+// [M, K] (scale = absmax / 127, the W8A8 tier, _int4/int8_eager.py:22-27).
+template <int G, int BITS>
 __global__ void __launch_bounds__(kQ5MaxThreads, 1)
 convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restrict__ qout,
                           float* __restrict__ scaleout, int M, int K, int rows_per_round) {
     static_assert(G == 64 || G == 256, "two-digit tiles only");
+    static_assert(BITS == 4 || BITS == 8, "int4 or int8 codes");
     extern __shared__ __align__(128) unsigned char q5smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(q5smem);
     uint32_t* rowmax = reinterpret_cast<uint32_t*>(q5smem + kQ5RowmaxOffset);   // [3][kQ5MaxTiles]
@@ -637,41 +640,82 @@ convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restric
         for (int i = tid; i < rows_per_round; i += blockDim.x) rowmax[((it + 2) % 3) * kQ5MaxTiles + i] = 0u;
 
         if (active) {
+            constexpr float kQMax = BITS == 4 ? 7.0f : 127.0f;
             const float amax = fmaxf(__uint_as_float(rmax[my_row]), Act<__nv_bfloat16>::floor_value());
-            const float sc = Act<__nv_bfloat16>::round(__fdiv_rn(amax, 7.0f));
+            const float sc = Act<__nv_bfloat16>::round(__fdiv_rn(amax, kQMax));
             const float rcp = __frcp_rn(sc);
             if (h == 0 && tile_in_row == 0) scaleout[row0 + my_row] = sc;
             const float2 rcp2 = make_float2(rcp, rcp);
-            const uint32_t magic = 0x43404340u;            // bf16 pair {192, 192}
-            uint32_t words[8][2];                           // per chunk: {a1 = 2h row, a1 = 2h+1 row}
-            #pragma unroll
-            for (int p = 0; p < 8; ++p) {
-                uint32_t tb[4];
+            const bool swap_b = kx & 1;                     // slot bh 0 holds columns 8..15
+            if constexpr (BITS == 4) {
+                const uint32_t magic = 0x43404340u;        // bf16 pair {192, 192}
+                uint32_t words[8][2];                       // per chunk: {a1 = 2h row, a1 = 2h+1 row}
                 #pragma unroll
-                for (int jj = 0; jj < 4; ++jj) {
-                    uint32_t c[2];
+                for (int p = 0; p < 8; ++p) {
+                    uint32_t tb[4];
+                    #pragma unroll
+                    for (int jj = 0; jj < 4; ++jj) {
+                        uint32_t c[2];
+                        #pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            const uint32_t y = packed[p][2 * jj + u];
+                            const float2 q = mul2(make_float2(__uint_as_float(y << 16), __uint_as_float(y & 0xFFFF0000u)), rcp2);
+                            c[u] = bf16x2_add(bf16x2_bits(q.x, q.y), magic) & 0x000F000Fu;
+                        }
+                        tb[jj] = c[0] | (c[1] << 4);            // byte 0: row 2h pair, byte 2: row 2h+1 pair
+                    }
+                    const uint32_t w01 = __byte_perm(tb[0], tb[1], 0x6240);
+                    const uint32_t w23 = __byte_perm(tb[2], tb[3], 0x6240);
+                    words[p][0] = __byte_perm(w01, w23, 0x5410);
+                    words[p][1] = __byte_perm(w01, w23, 0x7632);
+                }
+                int8_t* dst = qout + static_cast<size_t>(row0 + my_row) * (K >> 1) + tile_in_row * 128 + h * 64;
+                #pragma unroll
+                for (int a0s = 0; a0s < 4; ++a0s) {
+                    const int a0n = a0s ^ (kx >> 1);
                     #pragma unroll
                     for (int u = 0; u < 2; ++u) {
-                        const uint32_t y = packed[p][2 * jj + u];
-                        const float2 q = mul2(make_float2(__uint_as_float(y << 16), __uint_as_float(y & 0xFFFF0000u)), rcp2);
-                        c[u] = bf16x2_add(bf16x2_bits(q.x, q.y), magic) & 0x000F000Fu;
+                        const uint32_t w0 = words[2 * a0s][u], w1 = words[2 * a0s + 1][u];
+                        *reinterpret_cast<uint2*>(dst + (a0n + 4 * u) * 8) = swap_b ? make_uint2(w1, w0) : make_uint2(w0, w1);
                     }
-                    tb[jj] = c[0] | (c[1] << 4);                // byte 0: row 2h pair, byte 2: row 2h+1 pair
                 }
-                const uint32_t w01 = __byte_perm(tb[0], tb[1], 0x6240);
-                const uint32_t w23 = __byte_perm(tb[2], tb[3], 0x6240);
-                words[p][0] = __byte_perm(w01, w23, 0x5410);
-                words[p][1] = __byte_perm(w01, w23, 0x7632);
-            }
-            int8_t* dst = qout + static_cast<size_t>(row0 + my_row) * (K >> 1) + tile_in_row * 128 + h * 64;
-            const bool swap_b = kx & 1;                     // slot bh 0 holds columns 8..15
-            #pragma unroll
-            for (int a0s = 0; a0s < 4; ++a0s) {
-                const int a0n = a0s ^ (kx >> 1);
+            } else {
+                // t = bf16(y * fl(1/s)) as for int4; rint(t) by adding 1.5 * 2^23 in
+                // fp32 (exact for |t| < 2^22, ties to even), whose low bits hold the
+                // integer; clamp to +-127; one int8 per column, rows in order.
+                int8_t* dst = qout + static_cast<size_t>(row0 + my_row) * K + tile_in_row * 256 + h * 128;
                 #pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const uint32_t w0 = words[2 * a0s][u], w1 = words[2 * a0s + 1][u];
-                    *reinterpret_cast<uint2*>(dst + (a0n + 4 * u) * 8) = swap_b ? make_uint2(w1, w0) : make_uint2(w0, w1);
+                for (int a0s = 0; a0s < 4; ++a0s) {
+                    uint32_t rw[2][4];                          // [a1 row][16 columns as 4 words], slot order
+                    #pragma unroll
+                    for (int bh = 0; bh < 2; ++bh) {
+                        const int p = 2 * a0s + bh;
+                        int cv[2][8];
+                        #pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            const uint32_t y = packed[p][e];
+                            const float2 q = mul2(make_float2(__uint_as_float(y << 16), __uint_as_float(y & 0xFFFF0000u)), rcp2);
+                            const uint32_t tb = bf16x2_bits(q.x, q.y);
+                            const float2 r = add2(make_float2(__uint_as_float(tb << 16), __uint_as_float(tb & 0xFFFF0000u)),
+                                                  make_float2(12582912.0f, 12582912.0f));
+                            cv[0][e] = min(127, max(-127, static_cast<int>(__float_as_uint(r.x) - 0x4B400000u)));
+                            cv[1][e] = min(127, max(-127, static_cast<int>(__float_as_uint(r.y) - 0x4B400000u)));
+                        }
+                        #pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            rw[u][2 * bh] = __byte_perm(__byte_perm(cv[u][0], cv[u][1], 0x0040),
+                                                        __byte_perm(cv[u][2], cv[u][3], 0x0040), 0x5410);
+                            rw[u][2 * bh + 1] = __byte_perm(__byte_perm(cv[u][4], cv[u][5], 0x0040),
+                                                            __byte_perm(cv[u][6], cv[u][7], 0x0040), 0x5410);
+                        }
+                    }
+                    const int a0n = a0s ^ (kx >> 1);
+                    #pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        *reinterpret_cast<uint4*>(dst + (a0n + 4 * u) * 16) =
+                            swap_b ? make_uint4(rw[u][2], rw[u][3], rw[u][0], rw[u][1])
+                                   : make_uint4(rw[u][0], rw[u][1], rw[u][2], rw[u][3]);
+                    }
                 }
             }
         }
@@ -1016,10 +1060,10 @@ struct LoraArgs {
     float scale = 0.0f;
 };
 
-template <int BN, bool SWAP, int OUT, bool STAGED, bool LORA>
+template <int BN, bool SWAP, int OUT, bool STAGED, bool LORA, bool I8 = false>
 int launch_pair_impl(const void* Xp, const void* Wp, const float* xs, const float* ws, BiasRef bias,
                      void* out, int M, int N, int K, const LoraArgs& lora, cudaStream_t stream) {
-    using Cfg = PairCfg<BN, STAGED, SWAP, LORA>;
+    using Cfg = PairCfg<BN, STAGED, SWAP, LORA, I8>;
     const void* a_ptr = SWAP ? Wp : Xp;
     const void* b_ptr = SWAP ? Xp : Wp;
     const int rows_a = SWAP ? N : M;
@@ -1028,15 +1072,17 @@ int launch_pair_impl(const void* Xp, const void* Wp, const float* xs, const floa
     memset(&to, 0, sizeof(to));
     memset(&tlt, 0, sizeof(tlt));
     memset(&tlb, 0, sizeof(tlb));
-    if (!make_packed_tmap(&ta, a_ptr, rows_a, K, 128) ||
-        !make_packed_tmap(&tb, b_ptr, rows_b, K, BN / 2))
+    // (the packed-int4 map of 2K codes is the int8 map of K values: K bytes a row)
+    const int kcodes = I8 ? 2 * K : K;
+    if (!make_packed_tmap(&ta, a_ptr, rows_a, kcodes, 128) ||
+        !make_packed_tmap(&tb, b_ptr, rows_b, kcodes, BN / 2))
         return fail("cuTensorMapEncodeTiled failed (pointer not 16-byte aligned or driver entry point missing)");
     if (STAGED && !make_out_tmap(&to, out, M, N))
         return fail("cuTensorMapEncodeTiled failed for the output");
     if (LORA && (!make_bf16_tmap(&tlt, lora.t, M, lora.rank, 128) ||
                  !make_bf16_tmap(&tlb, lora.b, N, lora.rank, BN / 2)))
         return fail("cuTensorMapEncodeTiled failed for the LoRA operands");
-    auto kernel = int4_gemm_pair_kernel<BN, SWAP, OUT, STAGED, LORA>;
+    auto kernel = int4_gemm_pair_kernel<BN, SWAP, OUT, STAGED, LORA, I8>;
     cudaError_t e = ensure_smem(kernel, Cfg::kSmemBytes);
     if (e != cudaSuccess) return static_cast<int>(e);
     const int tiles_a = (rows_a + 255) / 256;
@@ -1156,6 +1202,21 @@ int dispatch_gemm(const void* Xp, const void* Wp, const float* xs, const float* 
     return launch_pair<256, false, OUT>(Xp, Wp, xs, ws, bias, out, M, N, K, stream);
 }
 
+// W8A8 tier: int8 X [M, K] and W [N, K] on CTA pairs (no swapped or few-token
+// forms: small M pays for a partly empty 256-row tile).
+template <int OUT>
+int dispatch_gemm_i8(const void* X, const void* W, const float* xs, const float* ws, BiasRef bias,
+                     void* out, int M, int N, int K, cudaStream_t stream) {
+    const long tiles256 = static_cast<long>((M + 255) / 256) * ((N + 255) / 256);
+    if (2 * tiles256 < sm_count() / 2)
+        return launch_pair_impl<128, false, OUT, false, false, true>(X, W, xs, ws, bias, out, M, N, K, LoraArgs(), stream);
+    if constexpr (OUT == kOutBF16) {
+        if ((N % 8) == 0 && aligned16(out) && K < 3072)    // under 24 stages a tile: staged stores
+            return launch_pair_impl<256, false, OUT, true, false, true>(X, W, xs, ws, bias, out, M, N, K, LoraArgs(), stream);
+    }
+    return launch_pair_impl<256, false, OUT, false, false, true>(X, W, xs, ws, bias, out, M, N, K, LoraArgs(), stream);
+}
+
 int check_gemm_args(const void* Xp, const void* Wp, int M, int N, int K) {
     if (M < 0 || N < 0 || K <= 0) return fail("M, N must be >= 0 and K > 0");
     if (K % 32 != 0) return fail("K must be a multiple of 32");
@@ -1193,7 +1254,7 @@ int launch_quant_t(const void* x, void* q, void* s, int M, int K, cudaStream_t s
 }
 
 // bf16 rows of whole 256-column tiles, G in {64, 256}: the two-threads-per-tile kernel.
-template <int G>
+template <int G, int BITS>
 int launch_quant_bf16_tiles(const void* x, void* q, void* s, int M, int K, cudaStream_t stream) {
     const int ntile = K / 256;
     // Rounds of about 96 tiles let two blocks share an SM (their phases drift
@@ -1207,7 +1268,7 @@ int launch_quant_bf16_tiles(const void* x, void* q, void* s, int M, int K, cudaS
     if (rows < 1) rows = 1;
     const int tiles = (rows * ntile + 15) / 16 * 16;
     const int smem = q5_smem_bytes(2 * tiles);
-    auto kernel = convrot_quant_bf16_kernel<G>;
+    auto kernel = convrot_quant_bf16_kernel<G, BITS>;
     cudaError_t e = ensure_smem(kernel, q5_smem_bytes(kQ5MaxThreads));
     if (e != cudaSuccess) return static_cast<int>(e);
     const int rounds = (M + rows - 1) / rows;
@@ -1221,7 +1282,7 @@ template <int G>
 int launch_quant_g(const void* x, int in_dtype, void* q, void* s, int M, int K, cudaStream_t stream) {
     if constexpr (G == 64 || G == 256) {
         if (in_dtype == 1 && K % 256 == 0 && K / 256 <= kQ5MaxTiles)
-            return launch_quant_bf16_tiles<G>(x, q, s, M, K, stream);
+            return launch_quant_bf16_tiles<G, 4>(x, q, s, M, K, stream);
     }
     switch (in_dtype) {
         case 0: return launch_quant_t<float, G>(x, q, s, M, K, stream);
@@ -1380,6 +1441,51 @@ CONVROT_API int ck_int4_gemm_s32(const void* Xp, const void* Wp, void* acc, int 
     if (!acc) return fail("null accumulator pointer");
     return dispatch_gemm<kOutS32>(Xp, Wp, nullptr, nullptr, BiasRef{nullptr, 0}, acc, M, N, K,
                                   static_cast<cudaStream_t>(stream));
+}
+
+CONVROT_API int ck_convrot_quant_int8(const void* x, int in_dtype, void* qout, void* scaleout,
+                                      int M, int K, int G, void* stream) {
+    if (!(G == 16 || G == 64 || G == 256)) return fail("G must be 16, 64 or 256");
+    if (K <= 0 || K % G != 0) return fail("K must be divisible by G");
+    if (int rc = check_quant_args(x, in_dtype, qout, scaleout, M, K)) return rc;
+    if (in_dtype != 1 || (G != 64 && G != 256) || K % 256 != 0 || K / 256 > kQ5MaxTiles)
+        return fail("the int8 quantizer takes bf16 rows of whole 256-column tiles with G = 64 or 256");
+    if (reinterpret_cast<uintptr_t>(qout) & 15u) return fail("qout must be 16-byte aligned");
+    if (M == 0) return 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (G == 256) return launch_quant_bf16_tiles<256, 8>(x, qout, scaleout, M, K, s);
+    return launch_quant_bf16_tiles<64, 8>(x, qout, scaleout, M, K, s);
+}
+
+int check_gemm_i8_args(const void* X, const void* W, int M, int N, int K) {
+    if (M < 0 || N < 0 || K <= 0) return fail("M, N must be >= 0 and K > 0");
+    if (K % 16 != 0) return fail("K must be a multiple of 16");
+    if (M > 0 && N > 0 && (!X || !W)) return fail("null operand pointer");
+    if (!aligned16(X) || !aligned16(W)) return fail("int8 operands must be 16-byte aligned");
+    return 0;
+}
+
+CONVROT_API int ck_int8_convrot_gemm(const void* X, const void* W, const void* xscale, const void* wscale,
+                                     const void* bias, void* out, int M, int N, int K, int out_dtype,
+                                     void* stream) {
+    if (int rc = check_gemm_i8_args(X, W, M, N, K)) return rc;
+    if (out_dtype != 0 && out_dtype != 1) return fail("out_dtype must be 0 (f32) or 1 (bf16)");
+    if (M == 0 || N == 0) return 0;
+    if (!xscale || !wscale || !out) return fail("null scale or output pointer");
+    const float* xs = static_cast<const float*>(xscale);
+    const float* ws = static_cast<const float*>(wscale);
+    const BiasRef b{bias, 0};
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (out_dtype == 1) return dispatch_gemm_i8<kOutBF16>(X, W, xs, ws, b, out, M, N, K, s);
+    return dispatch_gemm_i8<kOutF32>(X, W, xs, ws, b, out, M, N, K, s);
+}
+
+CONVROT_API int ck_int8_gemm_s32(const void* X, const void* W, void* acc, int M, int N, int K, void* stream) {
+    if (int rc = check_gemm_i8_args(X, W, M, N, K)) return rc;
+    if (M == 0 || N == 0) return 0;
+    if (!acc) return fail("null accumulator pointer");
+    return dispatch_gemm_i8<kOutS32>(X, W, nullptr, nullptr, BiasRef{nullptr, 0}, acc, M, N, K,
+                                     static_cast<cudaStream_t>(stream));
 }
 
 CONVROT_API int ck_convrot_device_status(void* stream, int* status) {

@@ -47,14 +47,18 @@ constexpr int kSwizzle128 = 2;           // tcgen05 descriptor code for 128-byte
 constexpr int kEpiThreads = 128;         // four epilogue warps
 constexpr uint32_t kEpiBarrier = 1;      // named barrier id of the epilogue warps
 
-template <int BN, bool STAGED, bool SWAP, bool LORA = false>
+// I8: the W8A8 tier -- plain int8 operands, no nibble expansion: both operands
+// go by TMA (cta_group::2, completing on the even CTA's barrier) straight into
+// shared memory and the MMAs read them there.
+template <int BN, bool STAGED, bool SWAP, bool LORA = false, bool I8 = false>
 struct PairCfg {
     static constexpr int kBHalf = BN / 2;
     static constexpr int kABytes = 128 * kPairBKP;
     static constexpr int kBBytes = kBHalf * kPairBKP;
-    static constexpr int kStageBytes = kABytes + 2 * kBBytes;
+    static constexpr int kStageBytes = I8 ? kABytes + kBBytes : kABytes + 2 * kBBytes;
     static constexpr int kTmemStageCols = 2 * kPairBKP / 4;      // hi + lo bytes of a row, 4 per column
-    static constexpr int kMmasPerStage = 2 * kPairBKP / 32;        // K = 32 bytes per MMA
+    static constexpr int kMmasPerStage = (I8 ? 1 : 2) * kPairBKP / 32;   // K = 32 bytes per MMA
+    static constexpr int kAccShift = I8 ? 0 : 8;                  // int4 halves accumulate 256 * D
     // bf16 output tile staged for the TMA store: 128 rows x BN cols, 64-col boxes
     static constexpr int kStagingBytes = STAGED ? 128 * BN * 2 : 0;
     // 227 KB per block, minus alignment slack, barriers and the staging tile
@@ -66,7 +70,7 @@ struct PairCfg {
     // TMA ring (shared memory) and expanded-A ring (TMEM slots) are sized
     // independently: the loads may run further ahead than TMEM allows.
     static constexpr int kAccCols = LORA ? 2 * BN : BN;          // int32 accumulator (+ fp32 LoRA accumulator)
-    static constexpr int kTmemStages0 = (static_cast<int>(kTmemCols) - kAccCols) / kTmemStageCols;
+    static constexpr int kTmemStages0 = I8 ? 16 : (static_cast<int>(kTmemCols) - kAccCols) / kTmemStageCols;
     static constexpr int kStagesBySmem = kSmemForStages / kStageBytes;
     static constexpr int kStagesCapped = kStagesBySmem < 16 ? kStagesBySmem : 16;
     // Swapped tiles: the three expander groups take TMA stages in turn, and TMA
@@ -95,6 +99,7 @@ struct PairCfg {
     static_assert(BN >= 32 && BN <= 256 && BN % 32 == 0, "pair MMA N must be a multiple of 32 in [32, 256]");
     static_assert(kStages >= 2 && kTmemStages >= 2, "pipeline needs at least two stages");
     static_assert(!SWAP || (kExpGroups == 3 && kStages % 3 == 0), "swapped tiles: ring slots owned by one group");
+    static_assert(!I8 || (!SWAP && !LORA), "the int8 tier uses plain, non-swapped tiles");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -151,7 +156,7 @@ __device__ __forceinline__ void store_row32(void* out, size_t obase, int n, int 
 // LORA (not swapped): a rank <= 64 side path out += lora_scale * T[m, :] . B[n, :]
 // (T = x A^T precomputed, both bf16) on the tensor cores into a second, fp32
 // accumulator, added in the epilogue before the single output rounding.
-template <int BN, bool SWAP, int OUT, bool STAGED, bool LORA = false>
+template <int BN, bool SWAP, int OUT, bool STAGED, bool LORA = false, bool I8 = false>
 __global__ void __launch_bounds__(kPairThreads, 1)
 int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_out,
@@ -159,7 +164,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                       const float* __restrict__ xscale, const float* __restrict__ wscale,
                       BiasRef bias, void* __restrict__ out, int M, int N, int K,
                       int tiles_a, int num_tiles, float lora_scale) {
-    using Cfg = PairCfg<BN, STAGED, SWAP, LORA>;
+    using Cfg = PairCfg<BN, STAGED, SWAP, LORA, I8>;
     static_assert(!LORA || !SWAP, "the LoRA side path is fused into non-swapped tiles");
     static_assert(!STAGED || (OUT == kOutBF16 && !SWAP), "staged epilogue is for bf16, non-swapped tiles");
     extern __shared__ __align__(1024) unsigned char psmem_raw[];
@@ -186,7 +191,8 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
     const uint32_t cta = cluster_ctarank();
     const int cluster_id = blockIdx.x >> 1;
     const int num_clusters = gridDim.x >> 1;
-    const int num_kt = ((K >> 1) + kPairBKP - 1) / kPairBKP;
+    const int row_bytes = I8 ? K : (K >> 1);                       // operand bytes per row
+    const int num_kt = (row_bytes + kPairBKP - 1) / kPairBKP;
     const int rows_a = SWAP ? N : M;
     // tiles of this cluster, and k-stage iterations over all of them
     const int my_tiles = (num_tiles - cluster_id + num_clusters - 1) / num_clusters;
@@ -261,9 +267,17 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                         record_status(kStatusTimeoutProducer); ok = false; break;
                     }
                     unsigned char* st = smem + s * Cfg::kStageBytes;
-                    mbar_arrive_expect_tx(&full_bar[s], Cfg::kABytes + Cfg::kBBytes);
-                    tma_load_2d(st, &tmap_a, &full_bar[s], kt * kPairBKP, a_row0);
-                    tma_load_2d(st + Cfg::kABytes, &tmap_b, &full_bar[s], kt * kPairBKP, b_row0);
+                    if constexpr (I8) {
+                        // both CTAs' tiles complete on the even CTA's barrier
+                        const uint32_t full_leader = mapa_shared(smem_u32(&full_bar[s]), 0);
+                        if (cta == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * (Cfg::kABytes + Cfg::kBBytes));
+                        tma_load_2d_pair(st, &tmap_a, full_leader, kt * kPairBKP, a_row0);
+                        tma_load_2d_pair(st + Cfg::kABytes, &tmap_b, full_leader, kt * kPairBKP, b_row0);
+                    } else {
+                        mbar_arrive_expect_tx(&full_bar[s], Cfg::kABytes + Cfg::kBBytes);
+                        tma_load_2d(st, &tmap_a, &full_bar[s], kt * kPairBKP, a_row0);
+                        tma_load_2d(st + Cfg::kABytes, &tmap_b, &full_bar[s], kt * kPairBKP, b_row0);
+                    }
                 }
             }
         }
@@ -281,6 +295,21 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                 for (int kt = 0; kt < num_kt; ++kt, ++it) {
                     const int s = it % Cfg::kStages;
                     const uint32_t ph = (it / Cfg::kStages) & 1;
+                    if constexpr (I8) {
+                        if (!mbar_wait_bounded<true>(&full_bar[s], ph)) {
+                            record_status(kStatusTimeoutMma); ok = false; break;
+                        }
+                        tc_fence_after();
+                        const uint32_t a_addr = smem_u32(smem + s * Cfg::kStageBytes);
+                        const uint32_t b_addr = a_addr + Cfg::kABytes;
+                        #pragma unroll
+                        for (int j = 0; j < Cfg::kMmasPerStage; ++j)
+                            mma_i8_ss_pair(tmem_base, smem_desc_kmajor(a_addr + j * 32, 8 * kPairBKP, kSwizzle128),
+                                           smem_desc_kmajor(b_addr + j * 32, 8 * kPairBKP, kSwizzle128),
+                                           Cfg::kIdesc, (kt | j) != 0);
+                        mma_commit_pair_multicast(&empty_bar[s], 0x3);
+                        continue;
+                    }
                     if (!mbar_wait_bounded<true>(&ready_bar[s], ph)) {
                         record_status(kStatusTimeoutMma); ok = false; break;
                     }
@@ -316,7 +345,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
             }
         }
     } else if (warp < 4) {
-        if (cta == 1 && lane == 0) {
+        if (!I8 && cta == 1 && lane == 0) {
             // ---------------- forwarders (odd CTA): local expansion done -> even CTA's MMA barrier
             const uint32_t ready_leader0 = mapa_shared(smem_u32(&ready_bar[0]), 0);
             for (int it = warp - 2; it < total_it; it += 2) {
@@ -326,7 +355,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                 mbar_arrive_cluster(ready_leader0 + s * 8);
             }
         }
-    } else if (warp < 12 || SWAP) {
+    } else if (!I8 && (warp < 12 || SWAP)) {
         // expansion done for stage s: local arrive (CTA-scope release)
         uint64_t* done_bar = (cta == 0) ? ready_bar : fwd_bar;
         const int quarter = warp & 3;
@@ -495,7 +524,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                         if (!lane_ok) continue;
                         #pragma unroll
                         for (int i = 0; i < 32; ++i) {
-                            const int32_t d = static_cast<int32_t>(acc[i]) >> 8;
+                            const int32_t d = static_cast<int32_t>(acc[i]) >> Cfg::kAccShift;
                             if constexpr (SWAP) {
                                 if (b + i < M) reinterpret_cast<int32_t*>(out)[static_cast<size_t>(b + i) * N + a] = d;
                             } else {
@@ -507,7 +536,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                         #pragma unroll
                         for (int i = 0; i < 32; ++i) {
                             if (b + i >= M) break;
-                            const float d = static_cast<float>(static_cast<int32_t>(acc[i]) >> 8);
+                            const float d = static_cast<float>(static_cast<int32_t>(acc[i]) >> Cfg::kAccShift);
                             const float v = __fmul_rn(__fmul_rn(d, cscale[col0 + i]), lane_scale);
                             const size_t o = static_cast<size_t>(b + i) * N + a;
                             if constexpr (OUT == kOutBF16)
@@ -521,7 +550,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                         float v[32];
                         #pragma unroll
                         for (int i = 0; i < 32; ++i) {
-                            const float d = static_cast<float>(static_cast<int32_t>(acc[i]) >> 8);
+                            const float d = static_cast<float>(static_cast<int32_t>(acc[i]) >> Cfg::kAccShift);
                             v[i] = __fmul_rn(__fmul_rn(d, lane_scale), cscale[col0 + i]);
                         }
                         if constexpr (LORA) {

@@ -233,6 +233,18 @@ __device__ __forceinline__ void mma_i8_ts_pair(uint32_t d_tmem, uint32_t a_tmem,
         : "memory");
 }
 
+// D (+)= A . B^T for a CTA pair, both int8 operands from shared memory
+// (descriptors of the issuing CTA's tiles; the peer's tiles at the same offsets).
+__device__ __forceinline__ void mma_i8_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+        :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrive once on the mbarrier at the same offset in every CTA of `cta_mask`
 // when all prior pair MMAs issued by this thread complete.
 __device__ __forceinline__ void mma_commit_pair_multicast(uint64_t* bar, uint16_t cta_mask) {

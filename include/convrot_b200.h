@@ -122,6 +122,34 @@ int ck_int4_convrot_gemm_splitk(const void* Xp, const void* Wp, const void* xsca
  * its GEMM (_int4/int4_gemm.hip:204-232); exposed for bit-exact parity checks. */
 int ck_int4_gemm_s32(const void* Xp, const void* Wp, void* acc, int M, int N, int K, void* stream);
 
+/* W8A8 tier (the int8 middle tier of mixed precision).
+ *
+ * Fused ConvRot rotation + row-wise int8 quantization, codes not packed.
+ * Replaces ck_convrot_quant_int8 (_int4/int4_gemm.hip:664-672), bound by
+ * convrot_quant_int8 (_int4/hip_loader.py:95-113); the quantizer arithmetic is
+ * the eager one in the activation dtype (_int4/int8_eager.py:22-27: scale =
+ * dtype(absmax / 127), q = rint(dtype(x / scale)) clamped to +-127).
+ *   x [M, K] (in_dtype must be 1 = bf16), qout [M, K] int8 (16-byte aligned),
+ *   scaleout [M] f32; G in {64, 256} and K % 256 == 0 (other dtypes, G = 16 or
+ *   ragged K return -1: the caller keeps its torch path, as the reference's
+ *   Python layer does for shapes its kernel does not take). */
+int ck_convrot_quant_int8(const void* x, int in_dtype, void* qout, void* scaleout,
+                          int M, int K, int G, void* stream);
+
+/* out[m, n] = ((float(D[m, n]) * xscale[m]) * wscale[n]) + bias[n],
+ * D = exact int32 sum_k X[m, k] * W[n, k] of int8 values.
+ * Replaces ck_int8_convrot_gemm (_int4/int4_gemm.hip:676-705), bound by
+ * int8_convrot_gemm (_int4/hip_loader.py:116-150).
+ *   X [M, K], W [N, K] int8 (16-byte aligned), xscale [M], wscale [N], bias [N]
+ *   or NULL: f32; out [M, N], out_dtype 0 = f32, 1 = bf16; K % 16 == 0. */
+int ck_int8_convrot_gemm(const void* X, const void* W, const void* xscale, const void* wscale,
+                         const void* bias, void* out, int M, int N, int K, int out_dtype,
+                         void* stream);
+
+/* Raw exact int32 accumulators of the int8 product (no reference export; for
+ * parity checks, like ck_int4_gemm_s32). */
+int ck_int8_gemm_s32(const void* X, const void* W, void* acc, int M, int N, int K, void* stream);
+
 /* Reads and clears the device status word that kernels set when a bounded
  * wait gives up (0 = ok). Synchronises `stream`. No reference counterpart:
  * the reference has no device-side timeouts. */

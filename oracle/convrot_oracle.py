@@ -40,6 +40,7 @@ import math
 import numpy as np
 
 INT4_MAX = 7
+INT8_MAX = 127
 QUANT_GROUP_SIZE = 64          # _int4/_codec.py:15 -- divisibility only, not a scale group
 SUPPORTED_GROUPS = (256, 64, 16)
 
@@ -183,14 +184,27 @@ def quantize_rowwise(xr: np.ndarray, dtype: str = "bf16") -> tuple[np.ndarray, n
 
     Returns (codes int8 [M, K] in [-7, 7], scale float32 [M]).
     """
+    return _quantize_rowwise(xr, dtype, INT4_MAX)
+
+
+def quantize_rowwise_int8(xr: np.ndarray, dtype: str = "bf16") -> tuple[np.ndarray, np.ndarray]:
+    """Eager row-wise symmetric int8 quantizer of the W8A8 tier
+    (``_int4/int8_eager.py:22-27``): the int4 arithmetic with 127 for 7.
+
+    Returns (codes int8 [M, K] in [-127, 127], scale float32 [M]).
+    """
+    return _quantize_rowwise(xr, dtype, INT8_MAX)
+
+
+def _quantize_rowwise(xr: np.ndarray, dtype: str, qmax: int) -> tuple[np.ndarray, np.ndarray]:
     v = to_f32(xr, dtype)
     absmax = np.abs(v).max(axis=1, keepdims=True) if v.shape[1] else np.zeros((v.shape[0], 1), np.float32)
     floor = round_to_dtype(np.array([1e-10], np.float32), dtype)[0]
     absmax = np.maximum(absmax, floor)
     with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
-        scale = round_to_dtype(absmax / np.float32(INT4_MAX), dtype)
+        scale = round_to_dtype(absmax / np.float32(qmax), dtype)
         t = round_to_dtype(v / scale, dtype)
-    q = np.clip(np.rint(t), -INT4_MAX, INT4_MAX).astype(np.int8)
+    q = np.clip(np.rint(t), -qmax, qmax).astype(np.int8)
     return q, scale.reshape(-1).astype(np.float32)
 
 
@@ -246,6 +260,22 @@ def int4_gemm_acc(xp: np.ndarray, wp: np.ndarray) -> np.ndarray:
     if xi.shape[1] >= 262144:
         raise ValueError("K too large for the exact float32 oracle")
     return (xi @ wi.T).astype(np.int32)
+
+
+def int8_gemm_acc(xq: np.ndarray, wq: np.ndarray) -> np.ndarray:
+    """Exact int32 accumulators D[m, n] = sum_k X[m,k] * W[n,k] of int8 values
+    (``_int4/int4_gemm.hip:421-492``). float64 BLAS is exact: |products| <= 2**14
+    and |D| < 2**31 < 2**53 for K <= 65536."""
+    xi = np.asarray(xq).astype(np.int8).astype(np.float64)
+    wi = np.asarray(wq).astype(np.int8).astype(np.float64)
+    if xi.shape[1] > 65536:
+        raise ValueError("K too large for int32 accumulators")
+    return (xi @ wi.T).astype(np.int32)
+
+
+def convrot_quant_int8(x: np.ndarray, group: int, dtype: str = "bf16") -> tuple[np.ndarray, np.ndarray]:
+    """W8A8 activation path: rotation, then the int8 quantizer (codes not packed)."""
+    return quantize_rowwise_int8(rotate(x, group, dtype), dtype)
 
 
 def int4_gemm_epilogue(acc: np.ndarray, xs: np.ndarray, ws: np.ndarray,
@@ -352,3 +382,11 @@ def dequantize_weight(wp: np.ndarray, ws: np.ndarray, group: int) -> np.ndarray:
     n, k = wi.shape
     h = hadamard(group)
     return (wi.reshape(n, k // group, group) @ h.T).reshape(n, k)
+
+
+def convrot_w8a8_linear(x: np.ndarray, qweight: np.ndarray, wscales: np.ndarray,
+                        bias: np.ndarray | None, group: int, dtype: str = "bf16") -> np.ndarray:
+    """W8A8 linear (``_int4/int8_eager.py:60-89`` with the int8 GEMM's exact int32
+    accumulator and fp32 epilogue, ``_int4/int4_gemm.hip:421-492``)."""
+    xq, xs = convrot_quant_int8(x, group, dtype)
+    return int4_gemm_epilogue(int8_gemm_acc(xq, qweight), xs, wscales, bias, dtype)

@@ -17,6 +17,11 @@ Reference functions exercised (paths relative to the reference project):
   _int4/eager.py:123-135  quantize_convrot_w4a4_weight (fp16 weight, as int4_ops.py:342-349)
   _int4/eager.py:154-169  int4_linear
   _int4/eager.py:172-197  convrot_w4a4_linear
+  _int4/int8_eager.py:22-27  quantize_signed_int8_rowwise (W8A8 tier)
+  _int4/int8_eager.py:30-47  quantize_convrot_w8a8_weight (fp16 weight, as int4_ops.py:339-342)
+  _int4/int8_eager.py:60-89  convrot_w8a8_linear
+
+``--only int8`` rewrites int8.npz alone.
 """
 from __future__ import annotations
 
@@ -65,10 +70,14 @@ def activation(gen: torch.Generator, m: int, k: int, outlier_frac: float = 0.01)
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the reference project checkout")
+    ap.add_argument("--only", choices=["int8"], default=None, help="write one file only")
     args = ap.parse_args()
     ref = load_reference(args.reference)
     eager, codec = ref.eager, ref._codec
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    if args.only == "int8":
+        write_int8(ref)
+        return
 
     # 1. codec: every nibble value at every position parity
     gen = torch.Generator().manual_seed(11)
@@ -134,7 +143,47 @@ def main() -> None:
         lin[f"{name}_out"] = bf16_bits(out)
         lin[f"{name}_meta"] = np.array([g, k, n, m])
     np.savez_compressed(os.path.join(HERE, "linear.npz"), **lin)
+    write_int8(ref)
     print("golden vectors written to", HERE)
+
+
+def write_int8(ref) -> None:
+    """5. the W8A8 tier (_int4/int8_eager.py): activation int8 quantization of the
+    rotated tensor, fp16 weight quantization and the eager W8A8 linear."""
+    eager, i8 = ref.eager, ref.int8_eager
+    out = {}
+    for name, g, k, dt in [("g256_bf16", 256, 768, torch.bfloat16), ("g64_bf16", 64, 512, torch.bfloat16),
+                           ("g16_bf16", 16, 160, torch.bfloat16), ("g256_f16", 256, 512, torch.float16),
+                           ("cfg0_bf16", 256, 3072, torch.bfloat16)]:
+        gen = torch.Generator().manual_seed(300 + k + g)
+        m = 40 if name != "cfg0_bf16" else 64
+        x = activation(gen, m, k).to(dt)
+        x[3] = 0                          # all-zero row -> absmax clamp
+        x[5] = 0
+        x[5, 7] = 3.0                     # single spike
+        h = eager._build_hadamard(g, device="cpu", dtype=dt)
+        xr = eager._rotate_activation(x, h, g).contiguous()
+        q, sc = i8.quantize_signed_int8_rowwise(xr)
+        out[f"q_{name}_x"] = store(x)
+        out[f"q_{name}_xrot"] = store(xr)
+        out[f"q_{name}_q"] = q.numpy()
+        out[f"q_{name}_scale"] = sc.numpy()
+        out[f"q_{name}_meta"] = np.array([g, k, {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}[dt]])
+    for name, g, k, n, m in [("g256", 256, 768, 96, 48), ("g64", 64, 512, 64, 33), ("cfg0", 256, 3072, 128, 64)]:
+        gen = torch.Generator().manual_seed(400 + k + n)
+        w = (torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16)
+        bias = (torch.randn(n, generator=gen) * 0.01).to(torch.bfloat16)
+        x = activation(gen, m, k).to(torch.bfloat16)
+        qw, ws = i8.quantize_convrot_w8a8_weight(w.to(torch.float16), g)
+        y = i8.convrot_w8a8_linear(x, qw, ws, bias=bias.to(torch.float16), convrot_groupsize=g)
+        out[f"l_{name}_w"] = bf16_bits(w)
+        out[f"l_{name}_bias"] = bf16_bits(bias)
+        out[f"l_{name}_x"] = bf16_bits(x)
+        out[f"l_{name}_qw"] = qw.numpy()
+        out[f"l_{name}_ws"] = ws.numpy()
+        out[f"l_{name}_out"] = bf16_bits(y)
+        out[f"l_{name}_meta"] = np.array([g, k, n, m])
+    np.savez_compressed(os.path.join(HERE, "int8.npz"), **out)
 
 
 if __name__ == "__main__":

@@ -176,3 +176,60 @@ def test_scale_multiply_identity_bf16():
     a = orc.bf16_bits_to_f32(np.arange(0x0001, 0x7F80, dtype=np.uint16))
     assert np.array_equal(orc.round_to_bf16(a / np.float32(7)),
                           orc.round_to_bf16(a * (np.float32(1) / np.float32(7))))
+
+
+# ------------------------------------------------------------------ W8A8 tier (int8.npz)
+
+I8_QUANT = ["g256_bf16", "g64_bf16", "g16_bf16", "g256_f16", "cfg0_bf16"]
+
+
+@pytest.mark.parametrize("case", I8_QUANT)
+def test_int8_quantizer_bit_exact_given_reference_rotation(case):
+    """The int8 quantizer (_int4/int8_eager.py:22-27) on the reference's rotated tensor."""
+    g = load("int8.npz")
+    dt = DTYPES[int(g[f"q_{case}_meta"][2])]
+    q, s = orc.quantize_rowwise_int8(g[f"q_{case}_xrot"], dt)
+    assert np.array_equal(q, g[f"q_{case}_q"])
+    assert np.array_equal(s.view(np.uint32), g[f"q_{case}_scale"].view(np.uint32))
+
+
+@pytest.mark.parametrize("case", I8_QUANT)
+def test_int8_codes_vs_reference_end_to_end(case):
+    """Kernel-order rotation + int8 quantizer: rotation ties move a code by at most one."""
+    g = load("int8.npz")
+    grp, _, dti = (int(v) for v in g[f"q_{case}_meta"])
+    dt = DTYPES[dti]
+    q, s = orc.convrot_quant_int8(g[f"q_{case}_x"], grp, dt)
+    diff = np.abs(q.astype(np.int32) - g[f"q_{case}_q"].astype(np.int32))
+    assert diff.max() <= 1
+    assert np.count_nonzero(diff) <= max(2, q.size // 20000)
+
+
+@pytest.mark.parametrize("case", ["g256", "g64", "cfg0"])
+def test_int8_linear_vs_reference(case):
+    """Exact int32 accumulator + fp32 epilogue vs the reference's eager W8A8 linear
+    (fp32 matmul of int8 values, then bf16): within 1e-2 relative L2."""
+    g = load("int8.npz")
+    grp, k, n, m = (int(v) for v in g[f"l_{case}_meta"])
+    x, qw, ws = g[f"l_{case}_x"], g[f"l_{case}_qw"], g[f"l_{case}_ws"]
+    bias = orc.bf16_bits_to_f32(g[f"l_{case}_bias"])
+    xq, xs = orc.convrot_quant_int8(x, grp, "bf16")
+    acc = orc.int8_gemm_acc(xq, qw)
+    assert np.array_equal(acc, xq.astype(np.int64) @ qw.astype(np.int64).T)
+    out = orc.bf16_bits_to_f32(orc.convrot_w8a8_linear(x, qw, ws, bias, grp))
+    ref = orc.bf16_bits_to_f32(g[f"l_{case}_out"])
+    rel = np.linalg.norm(out - ref) / np.linalg.norm(ref)
+    assert rel < 1e-2, rel
+
+
+@pytest.mark.parametrize("case", ["g256", "g64", "cfg0"])
+def test_int8_weight_quant_torch_matches_reference_bytes(case):
+    """_int4.int8_eager.quantize_convrot_w8a8_weight gives the reference's bytes."""
+    import torch
+    from _int4 import int8_eager
+    g = load("int8.npz")
+    grp = int(g[f"l_{case}_meta"][0])
+    w = torch.from_numpy(g[f"l_{case}_w"].view(np.int16)).view(torch.bfloat16).to(torch.float16)
+    qw, ws = int8_eager.quantize_convrot_w8a8_weight(w, grp)
+    assert np.array_equal(qw.numpy(), g[f"l_{case}_qw"])
+    assert np.array_equal(ws.numpy().view(np.uint32), g[f"l_{case}_ws"].view(np.uint32))
