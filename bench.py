@@ -46,9 +46,27 @@ LAYERS = [("qkv", 3072, 9216), ("attn_out", 3072, 3072), ("mlp_up", 3072, 12288)
 GROUP = 256
 LORA_RANK = 64
 
+def flux_dit_layers():
+    """Every int4 Linear of one forward of a Flux-architecture DiT (config 2): 19 double
+    blocks (image stream at 4096 tokens, text stream at 512) and 38 single blocks at
+    4608 tokens, hidden 3072, MLP x4; the modulation Linears run at M = 1. The
+    embedders and the final layer stay bf16 in the reference loader (EXCLUDED list)."""
+    layers = []
+    for d in range(19):
+        for stream, m in (("img", 4096), ("txt", 512)):
+            layers += [(f"d{d}.{stream}_attn.qkv", m, 3072, 9216, 0), (f"d{d}.{stream}_attn.proj", m, 3072, 3072, 0),
+                       (f"d{d}.{stream}_mlp.0", m, 3072, 12288, 0), (f"d{d}.{stream}_mlp.2", m, 12288, 3072, 0),
+                       (f"d{d}.{stream}_mod.lin", 1, 3072, 18432, 0)]
+    for b in range(38):
+        layers += [(f"s{b}.linear1", 4608, 3072, 21504, 0), (f"s{b}.linear2", 4608, 15360, 3072, 0),
+                   (f"s{b}.modulation.lin", 1, 3072, 9216, 0)]
+    return layers
+
+
 # Per-config step: (name, M, K, N, lora_rank). Config 1 is the default (the
 # BASELINE metric's configuration); the others are the BASELINE parity configs.
 WORKLOADS = {
+    2: ("config2_flux_dit_linears", flux_dit_layers()),
     0: ("config0_single_linear", [("linear", 512, 3072, 3072, 0)]),
     1: ("config1_flux_double_block_linears", [(name, M_TOKENS, k, n, 0) for name, k, n in LAYERS]),
     3: ("config3_zimage_mlp_token_sweep", [(f"{nm}_m{m}", m, k, n, 0) for m in (1024, 4096, 16384)
@@ -73,8 +91,14 @@ def layer_ops(m, k, n, r) -> int:
 
 def workload_config(cfg_id=1, extra=None):
     name, layers = WORKLOADS[cfg_id]
-    cfg = {"workload": name,
-           "layers": {lname: f"M={m} {k}->{n}" + (f" +LoRA r={r}" if r else "") for lname, m, k, n, r in layers},
+    if cfg_id == 2:
+        shapes = sorted({(m, k, n) for _, m, k, n, _ in layers}, reverse=True)
+        desc = {"linears": len(layers), "blocks": "19 double (img M=4096, txt M=512) + 38 single (M=4608)",
+                "shapes": [f"M={m} {k}->{n}" for m, k, n in shapes],
+                "weights": "random packed int4 codes and scales (the kernels' work does not depend on the values)"}
+    else:
+        desc = {"layers": {lname: f"M={m} {k}->{n}" + (f" +LoRA r={r}" if r else "") for lname, m, k, n, r in layers}}
+    cfg = {"workload": name, **desc,
            "convrot_groupsize": GROUP, "l2": "flushed before every timed step (256 MiB write)"}
     if cfg_id == 1:
         cfg.update({"tokens_per_gpu": M_TOKENS, "hidden": HIDDEN})
@@ -254,9 +278,16 @@ def build_layers(device, seed, cfg_id=1):
     gen = torch.Generator().manual_seed(seed)
     layers = []
     xs = {}
+    dgen = torch.Generator(device=device).manual_seed(seed)
     for name, m, k, n, r in WORKLOADS[cfg_id][1]:
-        w = (torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16).to(device)
-        qw, ws = _int4.quantize_convrot_w4a4_weight(w.to(torch.float16), GROUP)
+        if cfg_id == 2:
+            # 304 layers, 5.9 GB of int4 weights: random packed codes and scales
+            w = None
+            qw = torch.randint(-128, 128, (n, k // 2), generator=dgen, dtype=torch.int8, device=device)
+            ws = torch.rand(n, generator=dgen, device=device) * 1e-3 + 1e-5
+        else:
+            w = (torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16).to(device)
+            qw, ws = _int4.quantize_convrot_w4a4_weight(w.to(torch.float16), GROUP)
         bias = (torch.randn(n, generator=gen) * 0.01).to(torch.bfloat16).to(torch.float16).to(device)
         layer = {"name": name, "m": m, "k": k, "n": n, "r": r, "qw": qw, "ws": ws, "bias": bias,
                  "bias32": bias.float().contiguous()}
@@ -483,8 +514,11 @@ def run_ours(args, rank, world, local_rank):
 
     # ---------------- end to end: host buffers in, host buffers out, through the public API
     host_in = {k: v.cpu().pin_memory() for k, v in xs.items()}
-    host_out = [torch.empty((l["m"], l["n_out"] if "n_out" in l else l["n"]), dtype=torch.bfloat16).pin_memory()
-                for l in layers]
+    # one pinned buffer per output shape (config 2 has 304 outputs of 9 shapes); every
+    # layer's output still crosses PCIe each step
+    out_shapes = [(l["m"], l["n_out"] if "n_out" in l else l["n"]) for l in layers]
+    host_buf = {sh: torch.empty(sh, dtype=torch.bfloat16).pin_memory() for sh in set(out_shapes)}
+    host_out = [host_buf[sh] for sh in out_shapes]
     h2d = sum(v.numel() * v.element_size() for v in host_in.values())
     d2h = sum(v.numel() * v.element_size() for v in host_out)
 
