@@ -70,7 +70,11 @@ struct PairCfg {
     // TMA ring (shared memory) and expanded-A ring (TMEM slots) are sized
     // independently: the loads may run further ahead than TMEM allows.
     static constexpr int kAccCols = LORA ? 2 * BN : BN;          // int32 accumulator (+ fp32 LoRA accumulator)
-    static constexpr int kTmemStages0 = I8 ? 16 : (static_cast<int>(kTmemCols) - kAccCols) / kTmemStageCols;
+    // Accumulator buffers: with two, the next tile's MMAs run while the epilogue
+    // drains the previous tile (the int8 tier has no A operand in TMEM, so both fit).
+    static constexpr int kAccBufs = I8 ? 2 : 1;
+    static constexpr int kTmemStages0 =
+        I8 ? 16 : (static_cast<int>(kTmemCols) - kAccCols * kAccBufs) / kTmemStageCols;
     static constexpr int kStagesBySmem = kSmemForStages / kStageBytes;
     static constexpr int kStagesCapped = kStagesBySmem < 16 ? kStagesBySmem : 16;
     // Swapped tiles: the three expander groups take TMA stages in turn, and TMA
@@ -84,7 +88,7 @@ struct PairCfg {
     static constexpr int kStagingOffset = kStages * kStageBytes;
     static constexpr int kLoraOffset = kStagingOffset + kStagingBytes;
     static constexpr int kBarOffset = kLoraOffset + kLoraTBytes + kLoraBBytes;
-    static constexpr int kNumBars = 4 * kStages + kTmemStages + 4;
+    static constexpr int kNumBars = 4 * kStages + kTmemStages + 6;
     static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
     // per-tile column factors (scale, bias) x 2 tiles in flight
     static constexpr int kColOffset = kMiscOffset + 16;
@@ -176,10 +180,10 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
     uint64_t* empty_bar = bars + 2 * Cfg::kStages;
     uint64_t* fwd_bar = bars + 3 * Cfg::kStages;
     uint64_t* tmem_free_bar = bars + 4 * Cfg::kStages;           // [kTmemStages]
-    uint64_t* acc_full_bar = tmem_free_bar + Cfg::kTmemStages;
-    uint64_t* acc_empty_bar = acc_full_bar + 1;
-    uint64_t* lora_full_bar = acc_full_bar + 2;                  // even CTA: both CTAs' LoRA tiles landed
-    uint64_t* lora_empty_bar = acc_full_bar + 3;                 // LoRA MMAs of the previous tile done
+    uint64_t* acc_full_bar = tmem_free_bar + Cfg::kTmemStages;   // [2] per accumulator buffer
+    uint64_t* acc_empty_bar = acc_full_bar + 2;                  // [2]
+    uint64_t* lora_full_bar = acc_full_bar + 4;                  // even CTA: both CTAs' LoRA tiles landed
+    uint64_t* lora_empty_bar = acc_full_bar + 5;                 // LoRA MMAs of the previous tile done
     unsigned char* lora_t = smem + Cfg::kLoraOffset;
     unsigned char* lora_b = lora_t + Cfg::kLoraTBytes;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kMiscOffset);
@@ -206,8 +210,10 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
             mbar_init(&fwd_bar[s], Cfg::kLocalArrivals);
         }
         for (int t = 0; t < Cfg::kTmemStages; ++t) mbar_init(&tmem_free_bar[t], 1);
-        mbar_init(acc_full_bar, 1);
-        mbar_init(acc_empty_bar, 2);          // one epilogue arrival from each CTA
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full_bar[b], 1);
+            mbar_init(&acc_empty_bar[b], 2);  // one epilogue arrival from each CTA
+        }
         mbar_init(lora_full_bar, 1);
         mbar_init(lora_empty_bar, 1);
         fence_mbar_init();
@@ -239,7 +245,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
     griddep_wait();
     griddep_launch_dependents();
     const uint32_t tmem_base = *tmem_slot;
-    const uint32_t tmem_a0 = tmem_base + Cfg::kAccCols;  // A stages follow the accumulator columns
+    const uint32_t tmem_a0 = tmem_base + Cfg::kAccCols * Cfg::kAccBufs;  // A stages follow the accumulators
     const uint32_t tmem_lora = tmem_base + BN;           // fp32 LoRA accumulator (LORA only)
 
     if (warp == 0) {
@@ -288,9 +294,11 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
             bool ok = true;
             constexpr int kHalfSteps = Cfg::kMmasPerStage / 2;
             for (int lt = 0; lt < my_tiles && ok; ++lt) {
-                if (lt > 0 && !mbar_wait_bounded<true>(acc_empty_bar, (lt - 1) & 1)) {
+                const int abuf = lt % Cfg::kAccBufs, ause = lt / Cfg::kAccBufs;
+                if (ause > 0 && !mbar_wait_bounded<true>(&acc_empty_bar[abuf], (ause - 1) & 1)) {
                     record_status(kStatusTimeoutMma); break;
                 }
+                const uint32_t acc_tmem = tmem_base + abuf * Cfg::kAccCols;
                 tc_fence_after();
                 for (int kt = 0; kt < num_kt; ++kt, ++it) {
                     const int s = it % Cfg::kStages;
@@ -304,7 +312,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                         const uint32_t b_addr = a_addr + Cfg::kABytes;
                         #pragma unroll
                         for (int j = 0; j < Cfg::kMmasPerStage; ++j)
-                            mma_i8_ss_pair(tmem_base, smem_desc_kmajor(a_addr + j * 32, 8 * kPairBKP, kSwizzle128),
+                            mma_i8_ss_pair(acc_tmem, smem_desc_kmajor(a_addr + j * 32, 8 * kPairBKP, kSwizzle128),
                                            smem_desc_kmajor(b_addr + j * 32, 8 * kPairBKP, kSwizzle128),
                                            Cfg::kIdesc, (kt | j) != 0);
                         mma_commit_pair_multicast(&empty_bar[s], 0x3);
@@ -320,7 +328,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                     for (int j = 0; j < Cfg::kMmasPerStage; ++j) {
                         const uint32_t b_addr = b_hi + (j / kHalfSteps) * Cfg::kBBytes + (j % kHalfSteps) * 32;
                         const uint64_t bd = smem_desc_kmajor(b_addr, 8 * kPairBKP, kSwizzle128);
-                        mma_i8_ts_pair(tmem_base, tmem_a0 + ts * Cfg::kTmemStageCols + j * 8, bd, Cfg::kIdesc,
+                        mma_i8_ts_pair(acc_tmem, tmem_a0 + ts * Cfg::kTmemStageCols + j * 8, bd, Cfg::kIdesc,
                                        (kt | j) != 0);
                     }
                     mma_commit_pair_multicast(&empty_bar[s], 0x3);
@@ -341,7 +349,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                         mma_commit_pair_multicast(lora_empty_bar, 0x3);
                     }
                 }
-                if (ok) mma_commit_pair_multicast(acc_full_bar, 0x3);
+                if (ok) mma_commit_pair_multicast(&acc_full_bar[abuf], 0x3);
             }
         }
     } else if (warp < 4) {
@@ -457,7 +465,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         const int quarter = warp & 3;
         const int et = threadIdx.x - 384;                       // 0..127
         const int r = quarter * 32 + lane;                      // row within the CTA tile
-        const uint32_t acc_empty_leader = mapa_shared(smem_u32(acc_empty_bar), 0);
+        const uint32_t acc_empty_leader0 = mapa_shared(smem_u32(acc_empty_bar), 0);
         for (int lt = 0; lt < my_tiles; ++lt) {
             const int t = cluster_id + lt * num_clusters;
             const int a_row0 = (t % tiles_a) * 256 + static_cast<int>(cta) * 128;
@@ -495,7 +503,8 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                 if (et == 0) bulk_wait_group_read0();
             }
             named_barrier_sync(kEpiBarrier, kEpiThreads);
-            if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded<true>(acc_full_bar, lt & 1))) {
+            const int abuf = lt % Cfg::kAccBufs, ause = lt / Cfg::kAccBufs;
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded<true>(&acc_full_bar[abuf], ause & 1))) {
                 if (lane == 0) record_status(kStatusTimeoutEpilogue);
                 break;
             }
@@ -507,7 +516,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                 uint32_t acc2[kChunks][32];
                 uint32_t lora2[kChunks][32];
                 __syncwarp();
-                const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + cc * 32;
+                const uint32_t taddr = tmem_base + abuf * Cfg::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16) + cc * 32;
                 tmem_ld_32x32b_x32(taddr, acc2[0]);
                 if constexpr (LORA) {
                     tmem_ld_32x32b_x32(tmem_lora + (static_cast<uint32_t>(quarter * 32) << 16) + cc * 32, lora2[0]);
@@ -596,8 +605,8 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
             if constexpr (STAGED) fence_proxy_async_smem();
             named_barrier_sync(kEpiBarrier, kEpiThreads);
             if (et == 0) {
-                if (cta == 0) mbar_arrive(acc_empty_bar);
-                else mbar_arrive_cluster(acc_empty_leader);
+                if (cta == 0) mbar_arrive(&acc_empty_bar[abuf]);
+                else mbar_arrive_cluster(acc_empty_leader0 + abuf * 8);
                 if constexpr (STAGED) {
                     for (int bx = 0; bx < BN / 64; ++bx) {
                         if (b_tile0 + bx * 64 < N && a_row0 < M)
