@@ -387,6 +387,7 @@ def time_kernel(fn, iters, flush, stream):
 def run_ours(args, rank, world, local_rank):
     import _int4
     from _int4 import cuda_loader as ck
+    from _int4 import weight_cache
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     assert _int4.is_available(), "libconvrot_b200.so must load on an sm_100 device"
@@ -462,35 +463,52 @@ def run_ours(args, rank, world, local_rank):
     if rank == 0 and cfg_id == 1 and not args.nsplit:
         peaks, peak_src = load_peaks()
         up = next(l for l in layers if l["name"] == "mlp_up")
-        xq, xsc = ck.convrot_quant_int4(xs[(up["m"], up["k"])], GROUP)
-        iters = 10
-        gemm_ms = time_kernel(lambda: ck.int4_convrot_gemm(xq, up["qw"], xsc, up["ws"], up["bias32"],
-                                                           torch.bfloat16), iters, flush, stream)
-        # 8 distinct activations (8 x 28 MB, well beyond L2), launched back to back
-        xq_in = [synth_activation(up["m"], up["k"], torch.Generator().manual_seed(100 + i), device) for i in range(8)]
-        quant_ms = time_kernel_batch([lambda x=x: ck.convrot_quant_int4(x, GROUP) for x in xq_in], iters, flush, stream)
-        del xq_in
         m, k, n = up["m"], up["k"], up["n"]
+        iters = 10
+        # time the kernels the public linear runs for this layer: with the
+        # unpacked-weight cache on (default) and M > 128 that is the int8 pair GEMM
+        # on sign-extended codes, else the int4 pair GEMM on packed codes
+        unpacked = weight_cache.enabled() and m >= _int4._UNPACKED_MIN_ROWS
+        if unpacked:
+            quant = ck.convrot_quant_int4_unpacked
+            wq = weight_cache.unpacked(up["qw"])
+            xq, xsc = quant(xs[(m, k)], GROUP)
+            gemm = lambda: ck.int8_convrot_gemm(xq, wq, xsc, up["ws"], up["bias32"], torch.bfloat16)
+            gemm_name, code_bytes = "int8 pair GEMM on unpacked int4 codes", 1
+            traffic_key = "int8_pair_unpacked_bytes_per_launch"
+        else:
+            quant = ck.convrot_quant_int4
+            xq, xsc = quant(xs[(m, k)], GROUP)
+            gemm = lambda: ck.int4_convrot_gemm(xq, up["qw"], xsc, up["ws"], up["bias32"], torch.bfloat16)
+            gemm_name, code_bytes = "int4_gemm_pair_kernel", 0.5
+            traffic_key = "int4_gemm_kernel_bytes_per_launch"
+        gemm_ms = time_kernel(gemm, iters, flush, stream)
+        # 8 distinct activations (8 x 28 MB, well beyond L2), launched back to back
+        xq_in = [synth_activation(m, k, torch.Generator().manual_seed(100 + i), device) for i in range(8)]
+        quant_ms = time_kernel_batch([lambda x=x: quant(x, GROUP) for x in xq_in], iters, flush, stream)
+        del xq_in
         gemm_ops = 2 * m * n * k
         int8_peak = 2.0 * peaks["bf16_tflops"]           # dense int8 rate = 2x bf16 on B200
         achieved = gemm_ops / (gemm_ms * 1e-3) / 1e12
         traffic = load_traffic()
         extras["roofline"] = {
-            "kernel": "int4_gemm_pair_kernel (MLP up 3072->12288, M=4608)",
+            "kernel": f"int4_gemm_pair_kernel, {gemm_name} (MLP up 3072->12288, M=4608)",
             "bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
             "frac": achieved / int8_peak,
             "peak_source": f"2 x {peak_src} bf16 burst ({peaks['bf16_tflops']} TFLOP/s): B200 dense int8 rate",
             "ms_per_launch": gemm_ms,
-            "traffic": traffic.get("int4_gemm_kernel_bytes_per_launch") if traffic else None,
-            "algorithmic_bytes": m * k // 2 + n * k // 2 + 4 * m + 4 * n + 4 * n + 2 * m * n,
+            "traffic": traffic.get(traffic_key) if traffic else None,
+            "algorithmic_bytes": int(code_bytes * (m * k + n * k)) + 4 * m + 4 * n + 4 * n + 2 * m * n,
         }
-        qbytes = 2 * m * k + m * k // 2 + 4 * m
+        qbytes = 2 * m * k + int(code_bytes * m * k) + 4 * m
         extras["quant_kernel"] = {
-            "kernel": "convrot_quant_bf16_kernel (K=3072, M=4608)", "bound": "hbm",
+            "kernel": f"convrot_quant_bf16_kernel{' (unpacked codes)' if unpacked else ''} (K=3072, M=4608)",
+            "bound": "hbm",
             "achieved": qbytes / (quant_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": qbytes / (quant_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "ms_per_launch": quant_ms,
             "timing": "8 launches back to back over distinct 28 MB inputs in one CUDA graph, per launch",
-            "traffic": traffic.get("convrot_quant_bf16_kernel_bytes_per_launch") if traffic else None,
+            "traffic": traffic.get("convrot_quant_unpacked_bytes_per_launch" if unpacked else
+                                   "convrot_quant_bf16_kernel_bytes_per_launch") if traffic else None,
         }
         # small-M (weight-bound) layer: Flux modulation 3072 -> 18432 at M = 1
         wsm = (torch.randn(18432, 3072, device=device) * 0.02).to(torch.float16)
@@ -631,9 +649,16 @@ def run_case(args):
     bias = torch.zeros(n, device=device)
     x = synth_activation(m, k, gen, device)
     xq, xsc = ck.convrot_quant_int4(x, GROUP)
+    if args.case.endswith("_unpacked"):
+        xq, xsc = ck.convrot_quant_int4_unpacked(x, GROUP)
+        qw = ck.int4_unpack(qw)
     for _ in range(args.iters):
         if args.case == "quant":
             ck.convrot_quant_int4(x, GROUP)
+        elif args.case == "quant_unpacked":
+            ck.convrot_quant_int4_unpacked(x, GROUP)
+        elif args.case == "mlp_up_unpacked":
+            ck.int8_convrot_gemm(xq, qw, xsc, ws, bias, torch.bfloat16)
         else:
             ck.int4_convrot_gemm(xq, qw, xsc, ws, bias, torch.bfloat16)
     torch.cuda.synchronize()
@@ -654,7 +679,7 @@ def main():
                     help="config 4's 12288->3072 layer split by output columns over the ranks (strong scaling)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="launch every kernel from the host each step instead of replaying a CUDA graph")
-    ap.add_argument("--case", choices=["mlp_up", "small_m", "quant"], default=None,
+    ap.add_argument("--case", choices=["mlp_up", "small_m", "quant", "mlp_up_unpacked", "quant_unpacked"], default=None,
                     help="run one kernel --iters times (profiling helper) instead of the benchmark")
     ap.add_argument("--iters", type=int, default=3)
     args = ap.parse_args()

@@ -18,7 +18,7 @@ from __future__ import annotations
 import torch
 
 from ._codec import _INT4_GROUP_SIZE
-from . import cuda_loader
+from . import cuda_loader, weight_cache
 from .cuda_loader import convrot_quant_int4, int4_convrot_gemm, int4_convrot_gemm_lora
 from .cuda_loader import convrot_quant_int8, int8_convrot_gemm
 from .cuda_loader import is_available as _lib_available
@@ -37,12 +37,21 @@ __all__ = [
     "convrot_w4a4_linear",
     "convrot_w8a8_linear",
     "convrot_w4a4_linear_lora",
+    "set_unpacked_weights",
     "is_available",
     "pick_groupsize",
 ]
 
 # Output dtypes the GEMM epilogue writes directly; others compute f32 then cast.
 _NATIVE_OUT = frozenset({torch.float32, torch.bfloat16})
+# Rows from which a layer runs on unpacked codes (int8 pipeline); fewer tokens
+# keep the packed paths, which read each weight once as int4.
+_UNPACKED_MIN_ROWS = 129
+
+
+def set_unpacked_weights(enabled: bool = True) -> None:
+    """Allow (default) or forbid the cached unpacked weight copies (2x weight bytes)."""
+    weight_cache.enable(enabled)
 
 
 def pick_groupsize(in_features: int) -> int | None:
@@ -99,7 +108,14 @@ def convrot_w4a4_linear(
     shape = x.shape
     x2d = x.reshape(-1, shape[-1]).contiguous()
     out_dtype = x.dtype if x.dtype in _NATIVE_OUT else torch.float32
-    out = cuda_loader.convrot_w4a4_linear(x2d, qweight, wscales, bias, out_dtype, convrot_groupsize)
+    if (weight_cache.enabled() and x2d.shape[0] >= _UNPACKED_MIN_ROWS
+            and cuda_loader.unpacked_path_supported(x2d, convrot_groupsize)):
+        # many tokens: both operands as int8 codes on the int8 tensor-core pipeline
+        # (same accumulators, same results); the weight's codes are cached
+        codes = weight_cache.unpacked(qweight)
+        out = cuda_loader.convrot_w4a4_linear_unpacked(x2d, codes, wscales, bias, out_dtype, convrot_groupsize)
+    else:
+        out = cuda_loader.convrot_w4a4_linear(x2d, qweight, wscales, bias, out_dtype, convrot_groupsize)
     if out.dtype != x.dtype:
         out = out.to(x.dtype)
     return out.reshape(*shape[:-1], qweight.shape[0])

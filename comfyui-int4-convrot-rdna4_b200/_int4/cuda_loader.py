@@ -36,6 +36,10 @@ _SIGNATURES = {
     "ck_convrot_quant_int8": [_P, _I, _P, _P, _I, _I, _I, _P],
     "ck_int8_convrot_gemm": [_P] * 6 + [_I] * 4 + [_P],
     "ck_int8_gemm_s32": [_P, _P, _P, _I, _I, _I, _P],
+    "ck_int4_unpack": [_P, _P, ctypes.c_longlong, _I, _P],
+    "ck_convrot_quant_int4_unpacked": [_P, _I, _P, _P, _I, _I, _I, _P],
+    "ck_convrot_w4a4_linear_unpacked_workspace_size": [_I, _I],
+    "ck_convrot_w4a4_linear_unpacked": [_P, _I, _P, _P, _P, _I, _P] + [_I] * 5 + [_P, ctypes.c_size_t, _P],
     "ck_convrot_device_status": [_P, ctypes.POINTER(ctypes.c_int)],
     "ck_convrot_last_error": [],
 }
@@ -55,7 +59,8 @@ def _load():
                 fn = getattr(lib, name)
                 fn.argtypes = argtypes
                 fn.restype = {"ck_convrot_last_error": ctypes.c_char_p,
-                              "ck_convrot_w4a4_linear_workspace_size": ctypes.c_size_t}.get(name, ctypes.c_int)
+                              "ck_convrot_w4a4_linear_workspace_size": ctypes.c_size_t,
+                              "ck_convrot_w4a4_linear_unpacked_workspace_size": ctypes.c_size_t}.get(name, ctypes.c_int)
             _lib = lib
     return _lib
 
@@ -359,3 +364,63 @@ def int8_gemm_s32(x_int8, w_int8):
     rc = lib.ck_int8_gemm_s32(x_int8.data_ptr(), w_int8.data_ptr(), acc.data_ptr(), m, n, k, _stream(x_int8))
     _check("ck_int8_gemm_s32", rc)
     return acc
+
+
+# --------------------------------------------------------------------- unpacked-code path
+
+
+def int4_unpack(packed: torch.Tensor) -> torch.Tensor:
+    """packed int4 [R, K/2] -> int8 codes [R, K] on the device (ck_int4_unpack)."""
+    lib = _load()
+    _require_cuda(packed)
+    packed = packed.contiguous()
+    rows, kp = packed.shape
+    codes = torch.empty((rows, 2 * kp), dtype=torch.int8, device=packed.device)
+    rc = lib.ck_int4_unpack(packed.data_ptr(), codes.data_ptr(), rows, 2 * kp, _stream(packed))
+    _check("ck_int4_unpack", rc)
+    return codes
+
+
+def unpacked_path_supported(x: torch.Tensor, convrot_groupsize: int) -> bool:
+    """Activations the unpacked-code quantizer takes (bf16 whole tiles, G = 64/256)."""
+    return int8_quant_supported(x, convrot_groupsize)
+
+
+def convrot_quant_int4_unpacked(x: torch.Tensor, convrot_groupsize: int):
+    """Rotation + int4 quantization with one int8 per code: (codes [M, K], scale f32 [M])."""
+    lib = _load()
+    _require_cuda(x)
+    x = x.contiguous()
+    m, k = x.shape
+    qout = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    scale = torch.empty((m,), dtype=torch.float32, device=x.device)
+    rc = lib.ck_convrot_quant_int4_unpacked(x.data_ptr(), _IN_DTYPE_CODE.get(x.dtype, -1), qout.data_ptr(),
+                                            scale.data_ptr(), m, k, convrot_groupsize, _stream(x))
+    _check("ck_convrot_quant_int4_unpacked", rc)
+    return qout, scale
+
+
+def convrot_w4a4_linear_unpacked(x, w_codes, w_scale, bias, out_dtype, convrot_groupsize: int = 256):
+    """The W4A4 linear on unpacked codes (ck_convrot_w4a4_linear_unpacked): x [M, K] bf16,
+    w_codes int8 [N, K] from int4_unpack; results identical to convrot_w4a4_linear."""
+    lib = _load()
+    if out_dtype not in _OUT_DTYPE_CODE:
+        raise ValueError(f"int4 gemm output dtype must be float32/bfloat16, got {out_dtype}")
+    _require_cuda(x, w_codes)
+    x = x.contiguous()
+    w_codes = w_codes.contiguous()
+    m, k = x.shape
+    n, kw = w_codes.shape
+    if kw != k:
+        raise ValueError(f"K mismatch: x {tuple(x.shape)} w {tuple(w_codes.shape)}")
+    w_scale = w_scale.to(torch.float32).contiguous()
+    bias, bias_ptr, bias_code = _bias_arg(bias)
+    out = torch.empty((m, n), dtype=out_dtype, device=x.device)
+    ws_bytes = lib.ck_convrot_w4a4_linear_unpacked_workspace_size(m, k)
+    workspace = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=x.device)
+    rc = lib.ck_convrot_w4a4_linear_unpacked(x.data_ptr(), _IN_DTYPE_CODE.get(x.dtype, -1), w_codes.data_ptr(),
+                                             w_scale.data_ptr(), bias_ptr, bias_code, out.data_ptr(),
+                                             _OUT_DTYPE_CODE[out_dtype], m, n, k, convrot_groupsize,
+                                             workspace.data_ptr(), ws_bytes, _stream(x))
+    _check("ck_convrot_w4a4_linear_unpacked", rc)
+    return out

@@ -511,14 +511,17 @@ __device__ __forceinline__ uint32_t bf16x2_add(uint32_t a, uint32_t b) {
     return d;
 }
 
-// BITS = 4: packed int4 codes [M, K/2] (scale = absmax / 7); BITS = 8: int8 codes
-// [M, K] (scale = absmax / 127, the W8A8 tier, _int4/int8_eager.py:22-27).
-template <int G, int BITS>
+// BITS = 4: int4 codes (scale = absmax / 7), packed [M, K/2], or with UNPACKED one
+// sign-extended int8 per code [M, K] (the operand form of the int8 tensor-core
+// GEMM); BITS = 8: int8 codes [M, K] (scale = absmax / 127, the W8A8 tier,
+// _int4/int8_eager.py:22-27).
+template <int G, int BITS, bool UNPACKED = false>
 __global__ void __launch_bounds__(kQ5MaxThreads, 1)
 convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restrict__ qout,
                           float* __restrict__ scaleout, int M, int K, int rows_per_round) {
     static_assert(G == 64 || G == 256, "two-digit tiles only");
     static_assert(BITS == 4 || BITS == 8, "int4 or int8 codes");
+    static_assert(!UNPACKED || BITS == 4, "int8 codes are never packed");
     extern __shared__ __align__(128) unsigned char q5smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(q5smem);
     uint32_t* rowmax = reinterpret_cast<uint32_t*>(q5smem + kQ5RowmaxOffset);   // [3][kQ5MaxTiles]
@@ -647,7 +650,7 @@ convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restric
             if (h == 0 && tile_in_row == 0) scaleout[row0 + my_row] = sc;
             const float2 rcp2 = make_float2(rcp, rcp);
             const bool swap_b = kx & 1;                     // slot bh 0 holds columns 8..15
-            if constexpr (BITS == 4) {
+            if constexpr (BITS == 4 && !UNPACKED) {
                 const uint32_t magic = 0x43404340u;        // bf16 pair {192, 192}
                 uint32_t words[8][2];                       // per chunk: {a1 = 2h row, a1 = 2h+1 row}
                 #pragma unroll
@@ -680,9 +683,10 @@ convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restric
                     }
                 }
             } else {
-                // t = bf16(y * fl(1/s)) as for int4; rint(t) by adding 1.5 * 2^23 in
+                // t = bf16(y * fl(1/s)) as above; rint(t) by adding 1.5 * 2^23 in
                 // fp32 (exact for |t| < 2^22, ties to even), whose low bits hold the
-                // integer; clamp to +-127; one int8 per column, rows in order.
+                // integer; clamp to +-7 / +-127; one int8 per column, rows in order.
+                constexpr int kQI = BITS == 4 ? 7 : 127;
                 int8_t* dst = qout + static_cast<size_t>(row0 + my_row) * K + tile_in_row * 256 + h * 128;
                 #pragma unroll
                 for (int a0s = 0; a0s < 4; ++a0s) {
@@ -698,8 +702,8 @@ convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restric
                             const uint32_t tb = bf16x2_bits(q.x, q.y);
                             const float2 r = add2(make_float2(__uint_as_float(tb << 16), __uint_as_float(tb & 0xFFFF0000u)),
                                                   make_float2(12582912.0f, 12582912.0f));
-                            cv[0][e] = min(127, max(-127, static_cast<int>(__float_as_uint(r.x) - 0x4B400000u)));
-                            cv[1][e] = min(127, max(-127, static_cast<int>(__float_as_uint(r.y) - 0x4B400000u)));
+                            cv[0][e] = min(kQI, max(-kQI, static_cast<int>(__float_as_uint(r.x) - 0x4B400000u)));
+                            cv[1][e] = min(kQI, max(-kQI, static_cast<int>(__float_as_uint(r.y) - 0x4B400000u)));
                         }
                         #pragma unroll
                         for (int u = 0; u < 2; ++u) {
@@ -719,6 +723,33 @@ convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restric
                 }
             }
         }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// (1c) packed int4 -> one sign-extended int8 per code (column order kept)
+// ---------------------------------------------------------------------------
+// The operand form of the int8 tensor-core GEMM: with both operands unpacked,
+// sum_k x_k w_k is the int8 product over the same K, so the int4 layer runs on
+// the int8 pipeline with the exact same accumulators. HBM bound, run once per
+// weight tensor.
+__global__ void __launch_bounds__(256)
+int4_unpack_kernel(const uint4* __restrict__ packed, uint4* __restrict__ codes, size_t n16) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n16;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const uint4 v = packed[i];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t o[8];
+        #pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            // nibble n in [0, 15] -> n - 16 * (n >= 8): per byte (n ^ 8) - 8
+            const uint32_t lo = __vsub4((w[e] & 0x0F0F0F0Fu) ^ 0x08080808u, 0x08080808u);
+            const uint32_t hi = __vsub4(((w[e] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u, 0x08080808u);
+            o[2 * e] = __byte_perm(lo, hi, 0x5140);        // column 2j, 2j+1 of bytes 0, 1
+            o[2 * e + 1] = __byte_perm(lo, hi, 0x7362);    // of bytes 2, 3
+        }
+        codes[2 * i] = make_uint4(o[0], o[1], o[2], o[3]);
+        codes[2 * i + 1] = make_uint4(o[4], o[5], o[6], o[7]);
     }
 }
 
@@ -1254,7 +1285,7 @@ int launch_quant_t(const void* x, void* q, void* s, int M, int K, cudaStream_t s
 }
 
 // bf16 rows of whole 256-column tiles, G in {64, 256}: the two-threads-per-tile kernel.
-template <int G, int BITS>
+template <int G, int BITS, bool UNPACKED = false>
 int launch_quant_bf16_tiles(const void* x, void* q, void* s, int M, int K, cudaStream_t stream) {
     const int ntile = K / 256;
     // Rounds of about 96 tiles let two blocks share an SM (their phases drift
@@ -1268,7 +1299,7 @@ int launch_quant_bf16_tiles(const void* x, void* q, void* s, int M, int K, cudaS
     if (rows < 1) rows = 1;
     const int tiles = (rows * ntile + 15) / 16 * 16;
     const int smem = q5_smem_bytes(2 * tiles);
-    auto kernel = convrot_quant_bf16_kernel<G, BITS>;
+    auto kernel = convrot_quant_bf16_kernel<G, BITS, UNPACKED>;
     cudaError_t e = ensure_smem(kernel, q5_smem_bytes(kQ5MaxThreads));
     if (e != cudaSuccess) return static_cast<int>(e);
     const int rounds = (M + rows - 1) / rows;
@@ -1486,6 +1517,77 @@ CONVROT_API int ck_int8_gemm_s32(const void* X, const void* W, void* acc, int M,
     if (!acc) return fail("null accumulator pointer");
     return dispatch_gemm_i8<kOutS32>(X, W, nullptr, nullptr, BiasRef{nullptr, 0}, acc, M, N, K,
                                      static_cast<cudaStream_t>(stream));
+}
+
+CONVROT_API int ck_int4_unpack(const void* packed, void* codes, long long rows, int K, void* stream) {
+    if (rows < 0 || K <= 0 || K % 32 != 0) return fail("rows must be >= 0 and K a positive multiple of 32");
+    if (rows == 0) return 0;
+    if (!packed || !codes) return fail("null pointer");
+    if (!aligned16(packed) || !aligned16(codes)) return fail("packed and codes must be 16-byte aligned");
+    const size_t n16 = static_cast<size_t>(rows) * static_cast<size_t>(K / 2) / 16;
+    const int grid = static_cast<int>(n16 / 256 + 1 < static_cast<size_t>(4 * sm_count()) ? n16 / 256 + 1 : 4 * sm_count());
+    int4_unpack_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint4*>(packed), static_cast<uint4*>(codes), n16);
+    return static_cast<int>(cudaGetLastError());
+}
+
+namespace convrot {
+
+int check_unpacked_linear_args(const void* x, int in_dtype, int M, int K, int G) {
+    if (in_dtype != 1 || (G != 64 && G != 256) || K <= 0 || K % 256 != 0 || K / 256 > kQ5MaxTiles)
+        return fail("the unpacked-code path takes bf16 rows of whole 256-column tiles with G = 64 or 256");
+    if (M < 0) return fail("M must be >= 0");
+    if (M > 0 && !x) return fail("null pointer");
+    if (!aligned16(x)) return fail("x must be 16-byte aligned");
+    return 0;
+}
+
+size_t unpacked_linear_workspace_bytes(int M, int K) {
+    const size_t codes = (static_cast<size_t>(M) * static_cast<size_t>(K) + 255) & ~static_cast<size_t>(255);
+    return codes + ((static_cast<size_t>(M) * 4 + 255) & ~static_cast<size_t>(255));
+}
+
+}  // namespace convrot
+
+CONVROT_API int ck_convrot_quant_int4_unpacked(const void* x, int in_dtype, void* qout, void* scaleout,
+                                               int M, int K, int G, void* stream) {
+    if (int rc = check_unpacked_linear_args(x, in_dtype, M, K, G)) return rc;
+    if (M == 0) return 0;
+    if (!qout || !scaleout) return fail("null pointer");
+    if (reinterpret_cast<uintptr_t>(qout) & 15u) return fail("qout must be 16-byte aligned");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (G == 256) return launch_quant_bf16_tiles<256, 4, true>(x, qout, scaleout, M, K, s);
+    return launch_quant_bf16_tiles<64, 4, true>(x, qout, scaleout, M, K, s);
+}
+
+CONVROT_API size_t ck_convrot_w4a4_linear_unpacked_workspace_size(int M, int K) {
+    if (M <= 0 || K <= 0) return 0;
+    return unpacked_linear_workspace_bytes(M, K);
+}
+
+CONVROT_API int ck_convrot_w4a4_linear_unpacked(const void* x, int in_dtype, const void* Wcodes, const void* wscale,
+                                                const void* bias, int bias_dtype, void* out, int out_dtype,
+                                                int M, int N, int K, int G, void* workspace,
+                                                size_t workspace_bytes, void* stream) {
+    if (int rc = check_unpacked_linear_args(x, in_dtype, M, K, G)) return rc;
+    if (int rc = check_gemm_i8_args(x, Wcodes, M, N, K)) return rc;
+    if (out_dtype != 0 && out_dtype != 1) return fail("out_dtype must be 0 (f32) or 1 (bf16)");
+    if (bias_dtype < 0 || bias_dtype > 2) return fail("bias_dtype must be 0 (f32), 1 (bf16) or 2 (f16)");
+    if (M == 0 || N == 0) return 0;
+    if (!wscale || !out) return fail("null scale or output pointer");
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255u)) return fail("workspace must be 256-byte aligned");
+    if (workspace_bytes < unpacked_linear_workspace_bytes(M, K))
+        return fail("workspace smaller than ck_convrot_w4a4_linear_unpacked_workspace_size(M, K)");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    unsigned char* q = static_cast<unsigned char*>(workspace);
+    float* xs = reinterpret_cast<float*>(q + ((static_cast<size_t>(M) * K + 255) & ~static_cast<size_t>(255)));
+    int rc = G == 256 ? launch_quant_bf16_tiles<256, 4, true>(x, q, xs, M, K, s)
+                      : launch_quant_bf16_tiles<64, 4, true>(x, q, xs, M, K, s);
+    if (rc != 0) return rc;
+    const BiasRef b{bias, bias_dtype};
+    const float* ws = static_cast<const float*>(wscale);
+    if (out_dtype == 1) return dispatch_gemm_i8<kOutBF16>(q, Wcodes, xs, ws, b, out, M, N, K, s);
+    return dispatch_gemm_i8<kOutF32>(q, Wcodes, xs, ws, b, out, M, N, K, s);
 }
 
 CONVROT_API int ck_convrot_device_status(void* stream, int* status) {

@@ -150,6 +150,33 @@ int ck_int8_convrot_gemm(const void* X, const void* W, const void* xscale, const
  * parity checks, like ck_int4_gemm_s32). */
 int ck_int8_gemm_s32(const void* X, const void* W, void* acc, int M, int N, int K, void* stream);
 
+/* Unpacked-code path (no reference counterpart). With both operands as one
+ * sign-extended int8 per int4 code, sum_k x_k w_k is the int8 tensor-core product
+ * over the same K: bit-identical results to the packed path on the faster int8
+ * pipeline, at twice the bytes for the operands. */
+
+/* packed [rows, K/2] -> codes [rows, K] int8 (column order kept, nibbles
+ * sign-extended); both 16-byte aligned, K % 32 == 0. Run once per weight. */
+int ck_int4_unpack(const void* packed, void* codes, long long rows, int K, void* stream);
+
+/* ck_convrot_quant_int4 with unpacked output: codes [M, K] int8, scale [M] f32.
+ * bf16 rows of whole 256-column tiles, G in {64, 256}; -1 otherwise. */
+int ck_convrot_quant_int4_unpacked(const void* x, int in_dtype, void* qout, void* scaleout,
+                                   int M, int K, int G, void* stream);
+
+/* Workspace of ck_convrot_w4a4_linear_unpacked: align256(M * K) + align256(4 * M). */
+size_t ck_convrot_w4a4_linear_unpacked_workspace_size(int M, int K);
+
+/* ck_convrot_w4a4_linear with the weight given as unpacked codes Wcodes [N, K]
+ * int8 (from ck_int4_unpack): the quantizer writes unpacked activation codes to
+ * the workspace and the int8 pair GEMM (double-buffered accumulators) forms the
+ * exact products; same epilogue, same results. Same argument rules as
+ * ck_convrot_w4a4_linear plus those of ck_convrot_quant_int4_unpacked. */
+int ck_convrot_w4a4_linear_unpacked(const void* x, int in_dtype, const void* Wcodes, const void* wscale,
+                                    const void* bias, int bias_dtype, void* out, int out_dtype,
+                                    int M, int N, int K, int G, void* workspace, size_t workspace_bytes,
+                                    void* stream);
+
 /* Reads and clears the device status word that kernels set when a bounded
  * wait gives up (0 = ok). Synchronises `stream`. No reference counterpart:
  * the reference has no device-side timeouts. */

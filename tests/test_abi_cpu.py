@@ -111,6 +111,21 @@ def test_linear_rejects_bad_arguments(lib):
     assert call(m=0) == 0 and call(n=0) == 0                  # empty: nothing launched
 
 
+def test_unpacked_path_rejects_bad_arguments(lib):
+    assert lib.ck_convrot_w4a4_linear_unpacked_workspace_size(4608, 3072) == 4608 * 3072 + 4608 * 4
+    assert lib.ck_int4_unpack(16, 16, 4, 48, None) == -1                       # K % 32
+    assert lib.ck_int4_unpack(16, 17, 4, 64, None) == -1                       # alignment
+    assert lib.ck_int4_unpack(16, 16, 0, 64, None) == 0                        # empty
+    assert lib.ck_convrot_quant_int4_unpacked(16, 0, 16, 16, 4, 512, 256, None) == -1   # not bf16
+    assert lib.ck_convrot_quant_int4_unpacked(16, 1, 16, 16, 4, 320, 64, None) == -1    # ragged tile
+    f = lib.ck_convrot_w4a4_linear_unpacked
+    ws = lib.ck_convrot_w4a4_linear_unpacked_workspace_size(4, 256)
+    assert f(256, 1, 256, 256, 0, 0, 256, 1, 4, 8, 256, 16, 256, ws, None) == -1    # G = 16
+    assert f(256, 1, 256, 256, 0, 0, 256, 1, 4, 8, 256, 256, 256, ws - 1, None) == -1
+    assert b"workspace" in lib.ck_convrot_last_error()
+    assert f(256, 1, 256, 256, 0, 0, 256, 1, 0, 8, 256, 256, 256, ws, None) == 0
+
+
 def test_python_api_validation_errors():
     x = torch.zeros(4, 512, dtype=torch.bfloat16)
     qw = torch.zeros(8, 256, dtype=torch.int8)

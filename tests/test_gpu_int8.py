@@ -144,3 +144,56 @@ def test_w8a8_linear_other_shapes_take_torch_quant_then_native_gemm(ck):
     assert out.dtype == torch.float16
     rel = (out.float() - ref.float()).norm() / ref.float().norm()
     assert rel < 1e-2, rel
+
+
+# ------------------------------------------------------------------ unpacked-code path (int4 on the int8 pipeline)
+
+def test_int4_unpack_matches_codec(ck):
+    p = rand_i8(333, 1536, 9)                                   # packed [R, K/2]
+    codes = ck.int4_unpack(p)
+    torch.cuda.synchronize()
+    assert np.array_equal(codes.cpu().numpy(), orc.unpack_int4(p.cpu().numpy()))
+
+
+@pytest.mark.parametrize("m,k,g", [(129, 3072, 256), (300, 768, 64), (4608, 3072, 256), (5, 12288, 256)])
+def test_int4_quant_unpacked_equals_packed(ck, m, k, g):
+    x = activation(m, k, m + 3)
+    qu, su = ck.convrot_quant_int4_unpacked(x, g)
+    qp, sp = ck.convrot_quant_int4(x, g)
+    torch.cuda.synchronize()
+    assert torch.equal(su, sp)
+    assert np.array_equal(qu.cpu().numpy(), orc.unpack_int4(qp.cpu().numpy()))
+
+
+@pytest.mark.parametrize("m,k,n", [(129, 3072, 3072), (300, 768, 520), (4608, 3072, 12288), (1024, 12288, 3072),
+                                   (700, 3840, 15360)])
+@pytest.mark.parametrize("bias_dtype", [None, torch.float16, torch.float32])
+def test_int4_linear_unpacked_equals_packed(ck, m, k, n, bias_dtype):
+    g = torch.Generator().manual_seed(n)
+    x = activation(m, k, m)
+    wp = rand_i8(n, k // 2, n)
+    ws = (torch.rand(n, generator=g) * 0.01 + 1e-4).cuda()
+    bias = None if bias_dtype is None else (torch.randn(n, generator=g) * 0.1).to(bias_dtype).cuda()
+    a = ck.convrot_w4a4_linear_unpacked(x, ck.int4_unpack(wp), ws, bias, torch.bfloat16, 256)
+    b = ck.convrot_w4a4_linear(x, wp, ws, bias, torch.bfloat16, 256)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+def test_public_linear_takes_unpacked_path_for_many_tokens(ck):
+    import _int4
+    from _int4 import weight_cache
+    weight_cache.enable(True)
+    x = activation(512, 3072, 1)
+    w = (torch.randn(1024, 3072) * 0.02).to(torch.float16).cuda()
+    qw, ws = _int4.quantize_convrot_w4a4_weight(w, 256)
+    before = weight_cache.cached_bytes()
+    y = _int4.convrot_w4a4_linear(x, qw, ws)
+    assert weight_cache.cached_bytes() == before + 1024 * 3072
+    weight_cache.enable(False)
+    y_packed = _int4.convrot_w4a4_linear(x, qw, ws)
+    weight_cache.enable(True)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y_packed)
+    ora = orc.convrot_w4a4_linear(bits(x), qw.cpu().numpy(), ws.cpu().numpy(), None, 256)
+    assert np.array_equal(bits(y), ora)

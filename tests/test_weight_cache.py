@@ -1,0 +1,51 @@
+"""Host logic of the unpacked-weight cache (no GPU: a counting fake unpacker)."""
+import gc
+
+import torch
+
+from _int4 import weight_cache
+
+
+class CountingUnpack:
+    def __init__(self):
+        self.calls = 0
+
+    def __call__(self, packed):
+        self.calls += 1
+        return torch.zeros(packed.shape[0], 2 * packed.shape[1], dtype=torch.int8)
+
+
+def test_unpacked_once_per_tensor_and_refreshed_on_write():
+    weight_cache.enable(True)
+    f = CountingUnpack()
+    w = torch.zeros(8, 16, dtype=torch.int8)
+    a = weight_cache.unpacked(w, f)
+    b = weight_cache.unpacked(w, f)
+    assert a is b and f.calls == 1
+    w.add_(1)                                  # in-place write: version counter moves
+    c = weight_cache.unpacked(w, f)
+    assert c is not a and f.calls == 2
+    other = torch.zeros(8, 16, dtype=torch.int8)
+    weight_cache.unpacked(other, f)
+    assert f.calls == 3
+
+
+def test_copy_dropped_with_its_tensor():
+    weight_cache.enable(True)
+    f = CountingUnpack()
+    w = torch.zeros(4, 32, dtype=torch.int8)
+    weight_cache.unpacked(w, f)
+    before = weight_cache.cached_bytes()
+    assert before >= 4 * 64
+    del w
+    gc.collect()
+    assert weight_cache.cached_bytes() == before - 4 * 64
+
+
+def test_disable_frees_everything():
+    f = CountingUnpack()
+    keep = torch.zeros(2, 16, dtype=torch.int8)
+    weight_cache.unpacked(keep, f)
+    weight_cache.enable(False)
+    assert weight_cache.cached_bytes() == 0 and not weight_cache.enabled()
+    weight_cache.enable(True)
