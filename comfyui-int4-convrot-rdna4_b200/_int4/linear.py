@@ -2,31 +2,75 @@
 
 Mirrors ``Int4ConvRotOps.Linear.forward`` and ``_apply_dyn_lora``
 (int4_ops.py:366-383, :181-192) without ComfyUI: the weight is held as packed
-int4 codes ``_q`` [N, K/2] with per-row scales ``_qs`` [N] and an fp16 bias, and
-every forward runs the B200 kernels. Dynamic-LoRA adapters (down [r, K],
-up [N, r], alpha, strength) are fused into the GEMM epilogue instead of being
-added after it.
+int4 codes ``_q`` [N, K/2] (or int8 codes [N, K] for the W8A8 tier) with
+per-row scales ``_qs`` [N] and an fp16 bias, and every forward runs the B200
+kernels. Dynamic-LoRA adapters (down [r, K], up [N, r], alpha, strength) are
+fused into the int4 GEMM epilogue instead of being added after it.
+
+The state dict is the node's prequantized checkpoint form (``weight``,
+``weight_scale``, ``comfy_quant``, ``bias``; see ``_int4.checkpoint``), so
+``load_state_dict`` takes the tensors of a file the node saved and
+``state_dict`` gives back the same tensors.
 """
 from __future__ import annotations
 
 import torch
 
-from . import convrot_w4a4_linear, convrot_w4a4_linear_lora, pick_groupsize
+from . import checkpoint, convrot_w4a4_linear, convrot_w4a4_linear_lora, convrot_w8a8_linear, pick_groupsize
 from .eager import quantize_convrot_w4a4_weight
+
+_CKPT_KEYS = ("weight", "weight_scale", "comfy_quant", "bias")
 
 
 class Int4ConvRotLinear(torch.nn.Module):
     def __init__(self, in_features: int, out_features: int, bias: bool = True, device=None,
-                 convrot_groupsize: int | None = None):
+                 convrot_groupsize: int | None = None, mode: str = "int4"):
         super().__init__()
         g = convrot_groupsize or pick_groupsize(in_features)
         if g is None or in_features % 64:
             raise ValueError(f"in_features {in_features} is not quantizable (needs a multiple of 64)")
-        self.in_features, self.out_features, self._qgs = in_features, out_features, g
-        self.register_buffer("_q", torch.zeros(out_features, in_features // 2, dtype=torch.int8, device=device))
+        if mode not in ("int4", "int8"):
+            raise ValueError(f"mode must be 'int4' or 'int8', got {mode!r}")
+        self.in_features, self.out_features, self._qgs, self._qmode = in_features, out_features, g, mode
+        cols = in_features // 2 if mode == "int4" else in_features
+        self.register_buffer("_q", torch.zeros(out_features, cols, dtype=torch.int8, device=device))
         self.register_buffer("_qs", torch.ones(out_features, dtype=torch.float32, device=device))
         self.register_buffer("bias", torch.zeros(out_features, dtype=torch.float16, device=device) if bias else None)
         self._dyn_lora: list[tuple[torch.Tensor, torch.Tensor, float]] = []
+
+    # ---- checkpoint form (int4_ops.py:223-284 on load, int4_save.py:110-133 on save)
+    def _save_to_state_dict(self, destination, prefix, keep_vars):
+        def out(t):
+            return t if keep_vars else t.detach()
+        destination[prefix + "weight"] = out(self._q)
+        destination[prefix + "weight_scale"] = out(self._qs.reshape(-1, 1) if self._qmode == "int8" else self._qs)
+        destination[prefix + "comfy_quant"] = checkpoint.quant_tag(self._qmode, self._qgs)
+        if self.bias is not None:
+            destination[prefix + "bias"] = out(self.bias)
+
+    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys,
+                              unexpected_keys, error_msgs):
+        if strict:
+            for k in state_dict:
+                if k.startswith(prefix) and "." not in k[len(prefix):] and k[len(prefix):] not in _CKPT_KEYS:
+                    unexpected_keys.append(k)
+        if prefix + "weight" not in state_dict:
+            missing_keys.extend(prefix + k for k in ("weight", "weight_scale"))
+            return
+        had_bias = prefix + "bias" in state_dict
+        pw = checkpoint.take_prequantized(state_dict, prefix, self.in_features, device=self._qs.device)
+        if pw is None:
+            error_msgs.append(f"{prefix}weight: {tuple(state_dict[prefix + 'weight'].shape)} is not a ConvRot "
+                              f"int4/int8 layout for in_features={self.in_features}")
+            return
+        if pw.q.shape[0] != self.out_features or pw.scale.numel() != self.out_features:
+            error_msgs.append(f"{prefix}weight: {pw.q.shape[0]} rows, expected out_features={self.out_features}")
+            return
+        self._q, self._qs, self._qgs, self._qmode = pw.q, pw.scale, pw.groupsize, pw.mode
+        if pw.bias is not None:
+            self.bias = pw.bias
+        elif self.bias is not None and not had_bias:
+            missing_keys.append(prefix + "bias")
 
     @classmethod
     def from_linear(cls, linear: torch.nn.Linear, stochastic_rounding: int | None = 0,
@@ -53,6 +97,12 @@ class Int4ConvRotLinear(torch.nn.Module):
         self._dyn_lora = prepared
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self._qmode == "int8":
+            out = convrot_w8a8_linear(x, self._q, self._qs, self.bias, convrot_groupsize=self._qgs)
+            for down, up, scale in self._dyn_lora:        # fp16 low-rank side path, after the GEMM
+                h = torch.nn.functional.linear(torch.nn.functional.linear(x.half(), down.half()), up.half())
+                out = out + (h * scale).to(out.dtype)
+            return out
         if self._dyn_lora:
             return convrot_w4a4_linear_lora(x, self._q, self._qs, self.bias, self._dyn_lora, self._qgs)
         return convrot_w4a4_linear(x, self._q, self._qs, self.bias, convrot_groupsize=self._qgs)

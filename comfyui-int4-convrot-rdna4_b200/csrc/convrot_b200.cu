@@ -485,7 +485,10 @@ convrot_quant_kernel(const T* __restrict__ x, int8_t* __restrict__ qout, float* 
 
 constexpr int kQ5MaxThreads = 384;
 constexpr int kQ5MaxTiles = kQ5MaxThreads / 2;           // tiles per round, at most
-constexpr int kQ5PairTiles = 96;                         // round size that lets two blocks share an SM
+#ifndef CONVROT_Q5_ROUND_TILES
+#define CONVROT_Q5_ROUND_TILES 48
+#endif
+constexpr int kQ5RoundTiles = CONVROT_Q5_ROUND_TILES;    // target tiles per round (several blocks per SM)
 constexpr int kQ5RowmaxOffset = 16;
 constexpr int kQ5SlabOffset = 2432;                      // 16 + 3 * 192 * 4, to 128 B
 // shared memory of a block of `threads` threads: two slabs of threads / 2 tiles
@@ -603,20 +606,21 @@ convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restric
                 for (int e = 0; e < 8; ++e) h4x2(V[bh][e], V[bh + 2][e], V[bh + 4][e], V[bh + 6][e]);
             if constexpr (G == 256) {
                 // along a1, with the other half of the tile (lane ^ 16). Lane h
-                // holds {v_2h, v_2h+1}, receives the other pair r, and forms
-                // S = (v0+v1)+(v2+v3) (both lanes: sums commute) and its two
-                // outputs fma(-2, r.y, S), fma(-2, r.x, S).
+                // holds {v_2h, v_2h+1}; the lanes swap their pair sums, so both
+                // form S = (v0+v1)+(v2+v3) (sums commute), and lane h computes
+                // out_{3-2h} = fma(-2, v_2h, S) and out_{2-2h} = fma(-2, v_2h+1, S)
+                // from its own values: it ends up holding the rows a1 = 2h', 2h'+1
+                // of the other half h' = 1 - h, which is where it stores them.
                 #pragma unroll
                 for (int p = 0; p < 8; ++p) {
                     #pragma unroll
                     for (int e = 0; e < 8; ++e) {
                         const float2 v = V[p][e];
-                        const float ry = __shfl_xor_sync(mask, v.y, 16);
-                        const float rx = __shfl_xor_sync(mask, v.x, 16);
-                        const float s = __fadd_rn(__fadd_rn(v.x, v.y), __fadd_rn(rx, ry));
-                        float2 o = fma2(make_float2(-2.0f, -2.0f), make_float2(ry, rx), make_float2(s, s));
+                        const float own = __fadd_rn(v.x, v.y);
+                        const float s = __fadd_rn(own, __shfl_xor_sync(mask, own, 16));
+                        float2 o = fma2(make_float2(-2.0f, -2.0f), v, make_float2(s, s));
                         o = mul2(o, make_float2(0.0625f, 0.0625f));
-                        packed[p][e] = bf16x2_bits(o.x, o.y);
+                        packed[p][e] = bf16x2_bits(o.y, o.x);   // {row 2h', row 2h' + 1}
                     }
                 }
             } else {
@@ -650,6 +654,7 @@ convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restric
             if (h == 0 && tile_in_row == 0) scaleout[row0 + my_row] = sc;
             const float2 rcp2 = make_float2(rcp, rcp);
             const bool swap_b = kx & 1;                     // slot bh 0 holds columns 8..15
+            const int hs = G == 256 ? h ^ 1 : h;            // half of the tile whose rows this lane holds
             if constexpr (BITS == 4 && !UNPACKED) {
                 const uint32_t magic = 0x43404340u;        // bf16 pair {192, 192}
                 uint32_t words[8][2];                       // per chunk: {a1 = 2h row, a1 = 2h+1 row}
@@ -672,7 +677,7 @@ convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restric
                     words[p][0] = __byte_perm(w01, w23, 0x5410);
                     words[p][1] = __byte_perm(w01, w23, 0x7632);
                 }
-                int8_t* dst = qout + static_cast<size_t>(row0 + my_row) * (K >> 1) + tile_in_row * 128 + h * 64;
+                int8_t* dst = qout + static_cast<size_t>(row0 + my_row) * (K >> 1) + tile_in_row * 128 + hs * 64;
                 #pragma unroll
                 for (int a0s = 0; a0s < 4; ++a0s) {
                     const int a0n = a0s ^ (kx >> 1);
@@ -682,12 +687,50 @@ convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restric
                         *reinterpret_cast<uint2*>(dst + (a0n + 4 * u) * 8) = swap_b ? make_uint2(w1, w0) : make_uint2(w0, w1);
                     }
                 }
+            } else if constexpr (BITS == 4) {
+                // unpacked int4: the packed path's nibble (magic add of 192), sign
+                // extended within each 16-bit half, (n ^ 8) + 0xF8 = n - 8 mod 256
+                // in the low byte -- so the codes are those of the packed path for
+                // every input -- then one int8 per column, rows in order.
+                const uint32_t magic = 0x43404340u;
+                int8_t* dst = qout + static_cast<size_t>(row0 + my_row) * K + tile_in_row * 256 + hs * 128;
+                #pragma unroll
+                for (int a0s = 0; a0s < 4; ++a0s) {
+                    uint32_t rw[2][4];                          // [a1 row][16 columns as 4 words], slot order
+                    #pragma unroll
+                    for (int bh = 0; bh < 2; ++bh) {
+                        const int p = 2 * a0s + bh;
+                        uint32_t pr[4];                         // columns 2jj, 2jj+1: row 2h' in bytes 0-1, row 2h'+1 in 2-3
+                        #pragma unroll
+                        for (int jj = 0; jj < 4; ++jj) {
+                            uint32_t c[2];
+                            #pragma unroll
+                            for (int u = 0; u < 2; ++u) {
+                                const uint32_t y = packed[p][2 * jj + u];
+                                const float2 q = mul2(make_float2(__uint_as_float(y << 16), __uint_as_float(y & 0xFFFF0000u)), rcp2);
+                                c[u] = ((bf16x2_add(bf16x2_bits(q.x, q.y), magic) & 0x000F000Fu) ^ 0x00080008u) + 0x00F800F8u;
+                            }
+                            pr[jj] = __byte_perm(c[0], c[1], 0x6240);
+                        }
+                        rw[0][2 * bh] = __byte_perm(pr[0], pr[1], 0x5410);
+                        rw[1][2 * bh] = __byte_perm(pr[0], pr[1], 0x7632);
+                        rw[0][2 * bh + 1] = __byte_perm(pr[2], pr[3], 0x5410);
+                        rw[1][2 * bh + 1] = __byte_perm(pr[2], pr[3], 0x7632);
+                    }
+                    const int a0n = a0s ^ (kx >> 1);
+                    #pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        *reinterpret_cast<uint4*>(dst + (a0n + 4 * u) * 16) =
+                            swap_b ? make_uint4(rw[u][2], rw[u][3], rw[u][0], rw[u][1])
+                                   : make_uint4(rw[u][0], rw[u][1], rw[u][2], rw[u][3]);
+                    }
+                }
             } else {
-                // t = bf16(y * fl(1/s)) as above; rint(t) by adding 1.5 * 2^23 in
-                // fp32 (exact for |t| < 2^22, ties to even), whose low bits hold the
-                // integer; clamp to +-7 / +-127; one int8 per column, rows in order.
-                constexpr int kQI = BITS == 4 ? 7 : 127;
-                int8_t* dst = qout + static_cast<size_t>(row0 + my_row) * K + tile_in_row * 256 + h * 128;
+                // int8: t = bf16(y * fl(1/s)) as above; rint(t) by adding 1.5 * 2^23
+                // in fp32 (exact for |t| < 2^22, ties to even), whose low bits hold
+                // the integer; clamp to +-127; one int8 per column, rows in order.
+                constexpr int kQI = 127;
+                int8_t* dst = qout + static_cast<size_t>(row0 + my_row) * K + tile_in_row * 256 + hs * 128;
                 #pragma unroll
                 for (int a0s = 0; a0s < 4; ++a0s) {
                     uint32_t rw[2][4];                          // [a1 row][16 columns as 4 words], slot order
@@ -1288,19 +1331,24 @@ int launch_quant_t(const void* x, void* q, void* s, int M, int K, cudaStream_t s
 template <int G, int BITS, bool UNPACKED = false>
 int launch_quant_bf16_tiles(const void* x, void* q, void* s, int M, int K, cudaStream_t stream) {
     const int ntile = K / 256;
-    // Rounds of about 96 tiles let two blocks share an SM (their phases drift
-    // apart, which mixes the FMA-heavy rotation with the ALU-heavy packing);
-    // rows longer than that take one row per round.
-    const int blocks_per_sm = ntile <= kQ5PairTiles ? 2 : 1;
+    // Rounds of about kQ5RoundTiles tiles let several blocks share an SM (their
+    // phases drift apart, which mixes the FMA-heavy rotation with the ALU-heavy
+    // packing and the shared-memory loads); longer rows take one row per round.
+    int rows = kQ5RoundTiles / ntile;
+    if (rows < 1) rows = 1;
+    const int full_tiles = (rows * ntile + 15) / 16 * 16;
+    const int blocks_per_sm = full_tiles <= kQ5MaxTiles / 2 ? kQ5MaxTiles / full_tiles : 1;
     const int slots = blocks_per_sm * sm_count();
     const int per_block = (M + slots - 1) / slots;
-    int rows = (ntile <= kQ5PairTiles ? kQ5PairTiles : kQ5MaxTiles) / ntile;
     if (rows > per_block) rows = per_block;            // small M: spread the rows over the SMs
     if (rows < 1) rows = 1;
     const int tiles = (rows * ntile + 15) / 16 * 16;
     const int smem = q5_smem_bytes(2 * tiles);
     auto kernel = convrot_quant_bf16_kernel<G, BITS, UNPACKED>;
     cudaError_t e = ensure_smem(kernel, q5_smem_bytes(kQ5MaxThreads));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 static_cast<int>(cudaSharedmemCarveoutMaxShared));
     if (e != cudaSuccess) return static_cast<int>(e);
     const int rounds = (M + rows - 1) / rows;
     const int grid = rounds < slots ? rounds : slots;
