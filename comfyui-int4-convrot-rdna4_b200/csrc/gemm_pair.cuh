@@ -226,9 +226,11 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         tmem_alloc_pair(tmem_slot, kTmemCols);
         tmem_relinquish_pair();
     }
-    // The weight boxes of this CTA's first tile are pulled into L2 while the
-    // previous kernel may still be running (a hint: safe whatever it wrote).
-    if (warp == 0 && lane == 0 && cluster_id < num_tiles) {
+    // The weight boxes of this CTA's first tile are pulled into L2 (a hint:
+    // safe whatever the previous kernel wrote). The nibble-expanding forms do it
+    // here, while the previous kernel may still be running.
+    auto prefetch_first_weights = [&]() {
+        if (cluster_id >= num_tiles) return;
         const int t = cluster_id;
         if constexpr (SWAP) {
             const int w_row0 = (t % tiles_a) * 256 + static_cast<int>(cta) * 128;
@@ -237,13 +239,18 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
             const int w_row0 = (t / tiles_a) * BN + static_cast<int>(cta) * Cfg::kBHalf;
             for (int kt = 0; kt < num_kt; ++kt) tma_prefetch_l2_2d(&tmap_b, kt * kPairBKP, w_row0);
         }
-    }
+    };
+    if (!I8 && warp == 0 && lane == 0) prefetch_first_weights();
     tc_fence_before();
     cluster_sync();                       // peer barriers initialised before any remote arrive
     tc_fence_after();
     // every operand, scale and output may belong to the previous kernel
     griddep_wait();
     griddep_launch_dependents();
+    // int8 form: warp 3 has no role, so it pulls the weight boxes of this CTA's
+    // first tile into L2 ahead of the ring, after the sync (one prefetch per
+    // k-stage; issued before the sync they held every warp back).
+    if (I8 && warp == 3 && lane == 0) prefetch_first_weights();
     const uint32_t tmem_base = *tmem_slot;
     const uint32_t tmem_a0 = tmem_base + Cfg::kAccCols * Cfg::kAccBufs;  // A stages follow the accumulators
     const uint32_t tmem_lora = tmem_base + BN;           // fp32 LoRA accumulator (LORA only)
@@ -287,6 +294,46 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                 }
             }
         }
+    } else if (warp == 1 && I8) {
+        if (cta == 0) {
+            // ---------------- MMA issuer (even CTA), int8 form: the whole warp runs
+            // the loop, so the stage index, barrier phase and operand descriptors
+            // are warp-uniform values, and one elected lane issues the MMAs
+            int it = 0;
+            bool ok = true;
+            for (int lt = 0; lt < my_tiles && ok; ++lt) {
+                const int abuf = lt % Cfg::kAccBufs, ause = lt / Cfg::kAccBufs;
+                if (ause > 0 && !__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&acc_empty_bar[abuf], (ause - 1) & 1))) {
+                    if (lane == 0) record_status(kStatusTimeoutMma);
+                    break;
+                }
+                const uint32_t acc_tmem = tmem_base + abuf * Cfg::kAccCols;
+                tc_fence_after();
+                for (int kt = 0; kt < num_kt; ++kt, ++it) {
+                    const int s = it % Cfg::kStages;
+                    const uint32_t ph = (it / Cfg::kStages) & 1;
+                    if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&full_bar[s], ph))) {
+                        if (lane == 0) record_status(kStatusTimeoutMma);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + s * Cfg::kStageBytes);
+                    // K-major, 128 B swizzle: the j-th 32-byte K step is +2 in the address field
+                    const uint64_t da = smem_desc_kmajor(a_addr, 8 * kPairBKP, kSwizzle128);
+                    const uint64_t db = smem_desc_kmajor(a_addr + Cfg::kABytes, 8 * kPairBKP, kSwizzle128);
+                    if (elect_one()) {
+                        #pragma unroll
+                        for (int j = 0; j < Cfg::kMmasPerStage; ++j)
+                            mma_i8_ss_pair(acc_tmem, da + 2 * j, db + 2 * j, Cfg::kIdesc, (kt | j) != 0);
+                        mma_commit_pair_multicast(&empty_bar[s], 0x3);
+                    }
+                    __syncwarp();
+                }
+                if (ok && elect_one()) mma_commit_pair_multicast(&acc_full_bar[abuf], 0x3);
+                __syncwarp();
+            }
+        }
     } else if (warp == 1) {
         if (lane == 0 && cta == 0) {
             // ---------------- MMA issuer (even CTA)
@@ -303,21 +350,6 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                 for (int kt = 0; kt < num_kt; ++kt, ++it) {
                     const int s = it % Cfg::kStages;
                     const uint32_t ph = (it / Cfg::kStages) & 1;
-                    if constexpr (I8) {
-                        if (!mbar_wait_bounded<true>(&full_bar[s], ph)) {
-                            record_status(kStatusTimeoutMma); ok = false; break;
-                        }
-                        tc_fence_after();
-                        const uint32_t a_addr = smem_u32(smem + s * Cfg::kStageBytes);
-                        const uint32_t b_addr = a_addr + Cfg::kABytes;
-                        #pragma unroll
-                        for (int j = 0; j < Cfg::kMmasPerStage; ++j)
-                            mma_i8_ss_pair(acc_tmem, smem_desc_kmajor(a_addr + j * 32, 8 * kPairBKP, kSwizzle128),
-                                           smem_desc_kmajor(b_addr + j * 32, 8 * kPairBKP, kSwizzle128),
-                                           Cfg::kIdesc, (kt | j) != 0);
-                        mma_commit_pair_multicast(&empty_bar[s], 0x3);
-                        continue;
-                    }
                     if (!mbar_wait_bounded<true>(&ready_bar[s], ph)) {
                         record_status(kStatusTimeoutMma); ok = false; break;
                     }
