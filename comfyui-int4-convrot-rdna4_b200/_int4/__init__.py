@@ -147,30 +147,43 @@ def convrot_w4a4_linear_lora(
     _validate(x, qweight, convrot_groupsize, _INT4_GROUP_SIZE, "int4")
     shape = x.shape
     x2d = x.reshape(-1, shape[-1]).contiguous()
+    lora_t, up, scale = _lora_operands(x2d, adapters, qweight.shape[0])
+    out_dtype = x.dtype if x.dtype in _NATIVE_OUT else torch.float32
+    if (weight_cache.enabled() and x2d.shape[0] >= _UNPACKED_MIN_ROWS
+            and cuda_loader.unpacked_path_supported(x2d, convrot_groupsize)):
+        qact, x_scale = cuda_loader.convrot_quant_int4_unpacked(x2d, convrot_groupsize)
+        out = cuda_loader.int8_convrot_gemm_lora(qact, weight_cache.unpacked(qweight), x_scale, wscales, bias,
+                                                 out_dtype, lora_t, up, scale)
+    else:
+        qact, x_scale = convrot_quant_int4(x2d, convrot_groupsize)
+        out = int4_convrot_gemm_lora(qact, qweight, x_scale, wscales, bias, out_dtype, lora_t, up, scale)
+    if out.dtype != x.dtype:
+        out = out.to(x.dtype)
+    return out.reshape(*shape[:-1], qweight.shape[0])
+
+
+def _lora_operands(x2d: torch.Tensor, adapters, n: int):
+    """(T = x @ down^T [M, r] bf16, up [N, r] bf16, scale) for the fused side path;
+    several adapters are stacked along the rank, each scale folded into its up
+    matrix in bf16; the rank is padded to a multiple of 8."""
     if len(adapters) == 1:
         down, up, scale = adapters[0]
-        down = down.to(device=x.device, dtype=torch.bfloat16)
-        up = up.to(device=x.device, dtype=torch.bfloat16)
+        down = down.to(device=x2d.device, dtype=torch.bfloat16)
+        up = up.to(device=x2d.device, dtype=torch.bfloat16)
     else:
-        down = torch.cat([d.to(device=x.device, dtype=torch.bfloat16) for d, _, _ in adapters], dim=0)
-        up = torch.cat([(u.to(device=x.device, dtype=torch.float32) * float(s)).to(torch.bfloat16)
+        down = torch.cat([d.to(device=x2d.device, dtype=torch.bfloat16) for d, _, _ in adapters], dim=0)
+        up = torch.cat([(u.to(device=x2d.device, dtype=torch.float32) * float(s)).to(torch.bfloat16)
                         for _, u, s in adapters], dim=1)
         scale = 1.0
     rank = down.shape[0]
-    if rank > _MAX_LORA_RANK or up.shape != (qweight.shape[0], rank) or down.shape[1] != shape[-1]:
+    if rank > _MAX_LORA_RANK or up.shape != (n, rank) or down.shape[1] != x2d.shape[-1]:
         raise ValueError(f"LoRA down {tuple(down.shape)} / up {tuple(up.shape)} do not fit this layer "
                          f"(total rank must be <= {_MAX_LORA_RANK})")
     pad = (-rank) % 8
     if pad:
         down = torch.nn.functional.pad(down, (0, 0, 0, pad))
         up = torch.nn.functional.pad(up, (0, pad))
-    lora_t = x2d.to(torch.bfloat16) @ down.t()
-    qact, x_scale = convrot_quant_int4(x2d, convrot_groupsize)
-    out_dtype = x.dtype if x.dtype in _NATIVE_OUT else torch.float32
-    out = int4_convrot_gemm_lora(qact, qweight, x_scale, wscales, bias, out_dtype, lora_t, up, scale)
-    if out.dtype != x.dtype:
-        out = out.to(x.dtype)
-    return out.reshape(*shape[:-1], qweight.shape[0])
+    return x2d.to(torch.bfloat16) @ down.t(), up, scale
 
 
 def convrot_w8a8_linear(
@@ -188,21 +201,32 @@ def convrot_w8a8_linear(
     quantizer on the device, as the reference's layer does where its fused kernel does
     not apply. The product always runs on the int8 tensor cores (ck_int8_convrot_gemm).
     """
+    return convrot_w8a8_linear_lora(x, qweight, wscales, bias, (), convrot_groupsize)
+
+
+def convrot_w8a8_linear_lora(x, qweight, wscales, bias, adapters, convrot_groupsize: int = 256) -> torch.Tensor:
+    """``convrot_w8a8_linear`` plus Dynamic-LoRA side paths (as ``convrot_w4a4_linear_lora``)
+    fused into the int8 GEMM's epilogue; no adapters: the plain W8A8 linear."""
     if x.shape[-1] != qweight.shape[-1]:
         raise ValueError(f"Input K={x.shape[-1]} does not match qweight K={qweight.shape[-1]}")
     if x.shape[-1] % convrot_groupsize != 0:
         raise ValueError(f"Input K={x.shape[-1]} not divisible by convrot_groupsize {convrot_groupsize}")
     if not x.is_cuda:
         raise ValueError("the B200 ConvRot kernels need CUDA tensors")
+    adapters = list(adapters)
     shape = x.shape
     x2d = x.reshape(-1, shape[-1]).contiguous()
+    lora = _lora_operands(x2d, adapters, qweight.shape[0]) if adapters else None
     if cuda_loader.int8_quant_supported(x2d, convrot_groupsize):
         qact, x_scale = cuda_loader.convrot_quant_int8(x2d, convrot_groupsize)
     else:
         h = _build_hadamard(convrot_groupsize, device=x2d.device, dtype=x2d.dtype)
         qact, x_scale = _quantize_int8_rowwise(_rotate_activation(x2d, h, convrot_groupsize).contiguous())
     out_dtype = x.dtype if x.dtype in _NATIVE_OUT else torch.float32
-    out = cuda_loader.int8_convrot_gemm(qact, qweight, x_scale, wscales, bias, out_dtype)
+    if lora is not None:
+        out = cuda_loader.int8_convrot_gemm_lora(qact, qweight, x_scale, wscales, bias, out_dtype, *lora)
+    else:
+        out = cuda_loader.int8_convrot_gemm(qact, qweight, x_scale, wscales, bias, out_dtype)
     if out.dtype != x.dtype:
         out = out.to(x.dtype)
     return out.reshape(*shape[:-1], qweight.shape[0])

@@ -36,6 +36,7 @@ _SIGNATURES = {
     "ck_convrot_quant_int8": [_P, _I, _P, _P, _I, _I, _I, _P],
     "ck_int8_convrot_gemm": [_P] * 6 + [_I] * 4 + [_P],
     "ck_int8_gemm_s32": [_P, _P, _P, _I, _I, _I, _P],
+    "ck_int8_convrot_gemm_lora": [_P] * 5 + [_I, _P] + [_I] * 4 + [_P, _P, _I, ctypes.c_float, _P],
     "ck_int4_unpack": [_P, _P, ctypes.c_longlong, _I, _P],
     "ck_convrot_quant_int4_unpacked": [_P, _I, _P, _P, _I, _I, _I, _P],
     "ck_convrot_w4a4_linear_unpacked_workspace_size": [_I, _I],
@@ -159,10 +160,23 @@ def int4_convrot_gemm_lora(x_packed, w_packed, x_scale, w_scale, bias, out_dtype
 
     lora_t: bf16 [M, r] (= x @ A^T), lora_b: bf16 [N, r], r a multiple of 8 up to 64.
     """
+    x_packed, w_packed, m, n, k = _packed_pair(x_packed, w_packed)
+    return _gemm_lora("ck_int4_convrot_gemm_lora", x_packed, w_packed, m, n, k, x_scale, w_scale, bias,
+                      out_dtype, lora_t, lora_b, lora_scale)
+
+
+def int8_convrot_gemm_lora(x_int8, w_int8, x_scale, w_scale, bias, out_dtype, lora_t, lora_b, lora_scale):
+    """int4_convrot_gemm_lora on int8 operands [M, K] / [N, K] (the W8A8 tier, or
+    unpacked int4 codes: same accumulators, same output bits)."""
+    x_int8, w_int8, m, n, k = _int8_pair(x_int8, w_int8)
+    return _gemm_lora("ck_int8_convrot_gemm_lora", x_int8, w_int8, m, n, k, x_scale, w_scale, bias,
+                      out_dtype, lora_t, lora_b, lora_scale)
+
+
+def _gemm_lora(name, xq, wq, m, n, k, x_scale, w_scale, bias, out_dtype, lora_t, lora_b, lora_scale):
     lib = _load()
     if out_dtype not in _OUT_DTYPE_CODE:
-        raise ValueError(f"int4 gemm output dtype must be float32/bfloat16, got {out_dtype}")
-    x_packed, w_packed, m, n, k = _packed_pair(x_packed, w_packed)
+        raise ValueError(f"LoRA gemm output dtype must be float32/bfloat16, got {out_dtype}")
     _require_cuda(lora_t, lora_b)
     lora_t = lora_t.to(torch.bfloat16).contiguous()
     lora_b = lora_b.to(torch.bfloat16).contiguous()
@@ -171,13 +185,12 @@ def int4_convrot_gemm_lora(x_packed, w_packed, x_scale, w_scale, bias, out_dtype
         raise ValueError(f"LoRA shapes {tuple(lora_t.shape)} / {tuple(lora_b.shape)} do not match M={m}, N={n}")
     x_scale = x_scale.to(torch.float32).contiguous()
     w_scale = w_scale.to(torch.float32).contiguous()
-    out = torch.empty((m, n), dtype=out_dtype, device=x_packed.device)
+    out = torch.empty((m, n), dtype=out_dtype, device=xq.device)
     bias, bias_ptr, bias_code = _bias_arg(bias)
-    rc = lib.ck_int4_convrot_gemm_lora(x_packed.data_ptr(), w_packed.data_ptr(), x_scale.data_ptr(),
-                                       w_scale.data_ptr(), bias_ptr, bias_code, out.data_ptr(), m, n, k,
-                                       _OUT_DTYPE_CODE[out_dtype], lora_t.data_ptr(), lora_b.data_ptr(), r,
-                                       float(lora_scale), _stream(x_packed))
-    _check("ck_int4_convrot_gemm_lora", rc)
+    rc = getattr(lib, name)(xq.data_ptr(), wq.data_ptr(), x_scale.data_ptr(), w_scale.data_ptr(), bias_ptr,
+                            bias_code, out.data_ptr(), m, n, k, _OUT_DTYPE_CODE[out_dtype], lora_t.data_ptr(),
+                            lora_b.data_ptr(), r, float(lora_scale), _stream(xq))
+    _check(name, rc)
     return out
 
 

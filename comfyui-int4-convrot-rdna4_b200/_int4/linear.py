@@ -16,7 +16,8 @@ from __future__ import annotations
 
 import torch
 
-from . import checkpoint, convrot_w4a4_linear, convrot_w4a4_linear_lora, convrot_w8a8_linear, pick_groupsize
+from . import (checkpoint, convrot_w4a4_linear, convrot_w4a4_linear_lora, convrot_w8a8_linear_lora,
+               pick_groupsize)
 from .eager import quantize_convrot_w4a4_weight
 
 _CKPT_KEYS = ("weight", "weight_scale", "comfy_quant", "bias")
@@ -98,11 +99,7 @@ class Int4ConvRotLinear(torch.nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self._qmode == "int8":
-            out = convrot_w8a8_linear(x, self._q, self._qs, self.bias, convrot_groupsize=self._qgs)
-            for down, up, scale in self._dyn_lora:        # fp16 low-rank side path, after the GEMM
-                h = torch.nn.functional.linear(torch.nn.functional.linear(x.half(), down.half()), up.half())
-                out = out + (h * scale).to(out.dtype)
-            return out
+            return convrot_w8a8_linear_lora(x, self._q, self._qs, self.bias, self._dyn_lora, self._qgs)
         if self._dyn_lora:
             return convrot_w4a4_linear_lora(x, self._q, self._qs, self.bias, self._dyn_lora, self._qgs)
         return convrot_w4a4_linear(x, self._q, self._qs, self.bias, convrot_groupsize=self._qgs)

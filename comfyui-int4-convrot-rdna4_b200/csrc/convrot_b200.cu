@@ -1544,6 +1544,35 @@ int check_gemm_i8_args(const void* X, const void* W, int M, int N, int K) {
     return 0;
 }
 
+CONVROT_API int ck_int8_convrot_gemm_lora(const void* X, const void* W, const void* xscale, const void* wscale,
+                                          const void* bias, int bias_dtype, void* out, int M, int N, int K,
+                                          int out_dtype, const void* lora_t, const void* lora_b, int rank,
+                                          float lora_scale, void* stream) {
+    if (int rc = check_gemm_i8_args(X, W, M, N, K)) return rc;
+    if (out_dtype != 0 && out_dtype != 1) return fail("out_dtype must be 0 (f32) or 1 (bf16)");
+    if (bias_dtype < 0 || bias_dtype > 2) return fail("bias_dtype must be 0 (f32), 1 (bf16) or 2 (f16)");
+    if (rank < 8 || rank > 64 || rank % 8 != 0) return fail("LoRA rank must be a multiple of 8 in [8, 64]");
+    if (M == 0 || N == 0) return 0;
+    if (!xscale || !wscale || !out || !lora_t || !lora_b) return fail("null pointer");
+    if (!aligned16(lora_t) || !aligned16(lora_b)) return fail("LoRA operands must be 16-byte aligned");
+    LoraArgs lora;
+    lora.t = lora_t;
+    lora.b = lora_b;
+    lora.rank = rank;
+    lora.scale = lora_scale;
+    const float* xs = static_cast<const float*>(xscale);
+    const float* ws = static_cast<const float*>(wscale);
+    const BiasRef b{bias, bias_dtype};
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // 256 x 128 pair tiles: two buffers of (int32 + fp32 LoRA) accumulators fill TMEM
+    if (out_dtype == 1) {
+        if ((N % 8) == 0 && aligned16(out) && K < 3072)
+            return launch_pair_impl<128, false, kOutBF16, true, true, true>(X, W, xs, ws, b, out, M, N, K, lora, s);
+        return launch_pair_impl<128, false, kOutBF16, false, true, true>(X, W, xs, ws, b, out, M, N, K, lora, s);
+    }
+    return launch_pair_impl<128, false, kOutF32, false, true, true>(X, W, xs, ws, b, out, M, N, K, lora, s);
+}
+
 CONVROT_API int ck_int8_convrot_gemm(const void* X, const void* W, const void* xscale, const void* wscale,
                                      const void* bias, void* out, int M, int N, int K, int out_dtype,
                                      void* stream) {

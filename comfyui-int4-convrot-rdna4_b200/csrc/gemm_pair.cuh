@@ -103,7 +103,8 @@ struct PairCfg {
     static_assert(BN >= 32 && BN <= 256 && BN % 32 == 0, "pair MMA N must be a multiple of 32 in [32, 256]");
     static_assert(kStages >= 2 && kTmemStages >= 2, "pipeline needs at least two stages");
     static_assert(!SWAP || (kExpGroups == 3 && kStages % 3 == 0), "swapped tiles: ring slots owned by one group");
-    static_assert(!I8 || (!SWAP && !LORA), "the int8 tier uses plain, non-swapped tiles");
+    static_assert(!I8 || !SWAP, "the int8 form uses non-swapped tiles");
+    static_assert(!LORA || kAccBufs * kAccCols <= static_cast<int>(kTmemCols), "accumulators fit TMEM");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -253,7 +254,8 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
     if (I8 && warp == 3 && lane == 0) prefetch_first_weights();
     const uint32_t tmem_base = *tmem_slot;
     const uint32_t tmem_a0 = tmem_base + Cfg::kAccCols * Cfg::kAccBufs;  // A stages follow the accumulators
-    const uint32_t tmem_lora = tmem_base + BN;           // fp32 LoRA accumulator (LORA only)
+    // fp32 LoRA accumulator (LORA only): the second half of each accumulator buffer
+    auto tmem_lora = [&](int abuf) -> uint32_t { return tmem_base + abuf * Cfg::kAccCols + BN; };
 
     if (warp == 0) {
         if (lane == 0) {
@@ -330,6 +332,25 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                     }
                     __syncwarp();
                 }
+                if constexpr (LORA) {
+                    // the side path T . B^T on bf16 MMAs into this buffer's fp32 half
+                    if (ok && !__all_sync(0xFFFFFFFFu, mbar_wait_bounded(lora_full_bar, lt & 1))) {
+                        if (lane == 0) record_status(kStatusTimeoutMma);
+                        ok = false;
+                    }
+                    if (ok) {
+                        tc_fence_after();
+                        const uint64_t dt = smem_desc_kmajor(smem_u32(lora_t), 1024, kSwizzle128);
+                        const uint64_t dl = smem_desc_kmajor(smem_u32(lora_b), 1024, kSwizzle128);
+                        if (elect_one()) {
+                            #pragma unroll
+                            for (int j = 0; j < 4; ++j)    // rank 64 = four K = 16 bf16 steps of a 128 B row
+                                mma_bf16_ss_pair(tmem_lora(abuf), dt + 2 * j, dl + 2 * j, Cfg::kIdescLora, j != 0);
+                            mma_commit_pair_multicast(lora_empty_bar, 0x3);
+                        }
+                        __syncwarp();
+                    }
+                }
                 if (ok && elect_one()) mma_commit_pair_multicast(&acc_full_bar[abuf], 0x3);
                 __syncwarp();
             }
@@ -375,7 +396,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                         const uint32_t t_addr = smem_u32(lora_t), b_addr = smem_u32(lora_b);
                         #pragma unroll
                         for (int j = 0; j < 4; ++j)        // rank 64 = four K = 16 bf16 steps of a 128 B row
-                            mma_bf16_ss_pair(tmem_lora, smem_desc_kmajor(t_addr + 32 * j, 1024, kSwizzle128),
+                            mma_bf16_ss_pair(tmem_lora(abuf), smem_desc_kmajor(t_addr + 32 * j, 1024, kSwizzle128),
                                              smem_desc_kmajor(b_addr + 32 * j, 1024, kSwizzle128),
                                              Cfg::kIdescLora, j != 0);
                         mma_commit_pair_multicast(lora_empty_bar, 0x3);
@@ -551,7 +572,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                 const uint32_t taddr = tmem_base + abuf * Cfg::kAccCols + (static_cast<uint32_t>(quarter * 32) << 16) + cc * 32;
                 tmem_ld_32x32b_x32(taddr, acc2[0]);
                 if constexpr (LORA) {
-                    tmem_ld_32x32b_x32(tmem_lora + (static_cast<uint32_t>(quarter * 32) << 16) + cc * 32, lora2[0]);
+                    tmem_ld_32x32b_x32(tmem_lora(abuf) + (static_cast<uint32_t>(quarter * 32) << 16) + cc * 32, lora2[0]);
                 } else {
                     tmem_ld_32x32b_x32(taddr + 32, acc2[kChunks - 1]);
                 }

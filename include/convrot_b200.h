@@ -108,6 +108,16 @@ int ck_int4_convrot_gemm_lora(const void* Xp, const void* Wp, const void* xscale
                               int out_dtype, const void* lora_t, const void* lora_b, int rank,
                               float lora_scale, void* stream);
 
+/* ck_int4_convrot_gemm_lora on int8 operands X [M, K], W [N, K] (the W8A8 tier,
+ * or int4 codes sign-extended by ck_int4_unpack / ck_convrot_quant_int4_unpacked,
+ * which give the same D and so the same output bits); same epilogue, arguments
+ * and return codes. No reference counterpart (the reference's int8 layers add
+ * the LoRA side path after the GEMM, int4_ops.py:371-383). */
+int ck_int8_convrot_gemm_lora(const void* X, const void* W, const void* xscale, const void* wscale,
+                              const void* bias, int bias_dtype, void* out, int M, int N, int K,
+                              int out_dtype, const void* lora_t, const void* lora_b, int rank,
+                              float lora_scale, void* stream);
+
 /* accum[m, n] += (float(D[m, n]) * xscale[m]) * wscale[n] into a caller-zeroed
  * f32 [M, N] buffer. Replaces ck_int4_convrot_gemm_splitk
  * (_int4/int4_gemm.hip:634-645). The reference splits K and adds float

@@ -111,6 +111,14 @@ def test_linear_rejects_bad_arguments(lib):
     assert call(m=0) == 0 and call(n=0) == 0                  # empty: nothing launched
 
 
+def test_int8_lora_rejects_bad_arguments(lib):
+    f = lib.ck_int8_convrot_gemm_lora
+    assert f(16, 16, 16, 16, 0, 0, 16, 256, 256, 256, 1, 16, 16, 12, 1.0, None) == -1   # rank not a multiple of 8
+    assert f(16, 16, 16, 16, 0, 0, 16, 256, 256, 250, 1, 16, 16, 64, 1.0, None) == -1   # K % 16
+    assert f(16, 16, 16, 16, 0, 3, 16, 256, 256, 256, 1, 16, 16, 64, 1.0, None) == -1   # bias dtype
+    assert f(16, 16, 16, 16, 0, 0, 16, 0, 256, 256, 1, 16, 16, 64, 1.0, None) == 0      # empty
+
+
 def test_unpacked_path_rejects_bad_arguments(lib):
     assert lib.ck_convrot_w4a4_linear_unpacked_workspace_size(4608, 3072) == 4608 * 3072 + 4608 * 4
     assert lib.ck_int4_unpack(16, 16, 4, 48, None) == -1                       # K % 32

@@ -119,3 +119,71 @@ def test_lora_rejects_bad_rank(ck):
     lb = torch.zeros(n, 72, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(RuntimeError, match="rank"):
         ck.int4_convrot_gemm_lora(xp, wp, s[:m], s[:n], None, torch.bfloat16, lt, lb, 1.0)
+
+
+# ------------------------------------------------------------------ int8 operands (W8A8 tier, unpacked int4 codes)
+
+@pytest.mark.parametrize("m,n,k,r", [(256, 256, 512, 64), (300, 1000, 1024, 16), (1024, 3072, 3072, 64),
+                                     (129, 264, 256, 8), (700, 3072, 12288, 64)])
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+def test_int8_lora_on_unpacked_codes_equals_packed(ck, m, n, k, r, out_dtype):
+    """Same accumulators (sign-extended codes), same LoRA MMAs on the same 256 x 128
+    tiles, same epilogue: bit-identical to the packed kernel."""
+    g = torch.Generator().manual_seed(m * 3 + n + r)
+    xp = torch.randint(-128, 128, (m, k // 2), generator=g, dtype=torch.int8).cuda()
+    wp = torch.randint(-128, 128, (n, k // 2), generator=g, dtype=torch.int8).cuda()
+    xs = (torch.rand(m, generator=g) * 0.05 + 1e-3).cuda()
+    ws = (torch.rand(n, generator=g) * 0.01 + 1e-4).cuda()
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.float16).cuda()
+    lt = (torch.randn(m, r, generator=g) * 0.5).to(torch.bfloat16).cuda()
+    lb = (torch.randn(n, r, generator=g) * 0.01).to(torch.bfloat16).cuda()
+    a = ck.int8_convrot_gemm_lora(ck.int4_unpack(xp), ck.int4_unpack(wp), xs, ws, bias, out_dtype, lt, lb, 0.75)
+    b = ck.int4_convrot_gemm_lora(xp, wp, xs, ws, bias, out_dtype, lt, lb, 0.75)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+def test_public_lora_linear_many_tokens_takes_unpacked_path(ck):
+    import _int4
+    from _int4 import weight_cache
+    weight_cache.enable(True)
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(512, 3072, generator=g).to(torch.bfloat16).cuda()
+    w = (torch.randn(1024, 3072, generator=g) * 0.02).to(torch.float16).cuda()
+    qw, ws = _int4.quantize_convrot_w4a4_weight(w, 256)
+    ad = [((torch.randn(64, 3072, generator=g) * 0.01).cuda(), (torch.randn(1024, 64, generator=g) * 0.01).cuda(), 1.0)]
+    before = weight_cache.cached_bytes()
+    y = _int4.convrot_w4a4_linear_lora(x, qw, ws, None, ad)
+    assert weight_cache.cached_bytes() == before + 1024 * 3072
+    weight_cache.enable(False)
+    y_packed = _int4.convrot_w4a4_linear_lora(x, qw, ws, None, ad)
+    weight_cache.enable(True)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y_packed)
+
+
+def test_w8a8_lora_api_and_int8_module(ck):
+    """W8A8 tier with adapters: the side path fused into the int8 GEMM epilogue, against
+    the plain W8A8 linear plus an fp32 torch side path (1e-2 relative L2), also through
+    Int4ConvRotLinear in int8 mode."""
+    import _int4
+    from _int4 import int8_eager
+    from _int4.linear import Int4ConvRotLinear
+    m, k, n = 384, 768, 512
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).cuda()
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.float16).cuda()
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.float16).cuda()
+    qw, ws = int8_eager.quantize_convrot_w8a8_weight(w, 256)
+    a1 = ((torch.randn(32, k, generator=g) * 0.01).cuda(), (torch.randn(n, 32, generator=g) * 0.01).cuda(), 2.0)
+    base = _int4.convrot_w8a8_linear(x, qw, ws, bias).float()
+    side = 2.0 * ((x.float() @ a1[0].float().t()) @ a1[1].float().t())
+    out = _int4.convrot_w8a8_linear_lora(x, qw, ws, bias, [a1]).float()
+    ref = base + side
+    assert (out - ref).norm() / ref.norm() < 1e-2
+    assert (out - base).norm() / side.norm() > 0.9
+    mod = Int4ConvRotLinear(k, n, device="cuda")
+    mod.load_state_dict({"weight": qw, "weight_scale": ws, "bias": bias})
+    assert mod._qmode == "int8"
+    mod.set_dynamic_lora([(a1[0], a1[1], 64, 2.0 * 32 / 64)])       # alpha / r * strength = 2.0
+    assert torch.equal(mod(x), _int4.convrot_w8a8_linear_lora(x, qw, ws, bias, [a1]))
