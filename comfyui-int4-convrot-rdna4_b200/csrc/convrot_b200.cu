@@ -1564,12 +1564,20 @@ CONVROT_API int ck_int8_convrot_gemm_lora(const void* X, const void* W, const vo
     const float* ws = static_cast<const float*>(wscale);
     const BiasRef b{bias, bias_dtype};
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    // 256 x 128 pair tiles: two buffers of (int32 + fp32 LoRA) accumulators fill TMEM
+    // 256 x 256 pair tiles (one int32 + fp32 accumulator pair fills TMEM) halve the
+    // operand bytes per MMA of 256 x 128 tiles (two buffers, epilogue overlapped);
+    // the latter only when 256-column tiles leave most CTA pairs idle
+    const long tiles256 = static_cast<long>((M + 255) / 256) * ((N + 255) / 256);
+    const bool wide = 2 * tiles256 >= sm_count();
     if (out_dtype == 1) {
+        if (wide)
+            return launch_pair_impl<256, false, kOutBF16, false, true, true>(X, W, xs, ws, b, out, M, N, K, lora, s);
         if ((N % 8) == 0 && aligned16(out) && K < 3072)
             return launch_pair_impl<128, false, kOutBF16, true, true, true>(X, W, xs, ws, b, out, M, N, K, lora, s);
         return launch_pair_impl<128, false, kOutBF16, false, true, true>(X, W, xs, ws, b, out, M, N, K, lora, s);
     }
+    if (wide)
+        return launch_pair_impl<256, false, kOutF32, false, true, true>(X, W, xs, ws, b, out, M, N, K, lora, s);
     return launch_pair_impl<128, false, kOutF32, false, true, true>(X, W, xs, ws, b, out, M, N, K, lora, s);
 }
 

@@ -72,7 +72,8 @@ struct PairCfg {
     static constexpr int kAccCols = LORA ? 2 * BN : BN;          // int32 accumulator (+ fp32 LoRA accumulator)
     // Accumulator buffers: with two, the next tile's MMAs run while the epilogue
     // drains the previous tile (the int8 tier has no A operand in TMEM, so both fit).
-    static constexpr int kAccBufs = I8 ? 2 : 1;
+    // (256-column LoRA tiles need all 512 columns for one int32 + fp32 pair: one buffer)
+    static constexpr int kAccBufs = (I8 && !(LORA && BN > 128)) ? 2 : 1;
     static constexpr int kTmemStages0 =
         I8 ? 16 : (static_cast<int>(kTmemCols) - kAccCols * kAccBufs) / kTmemStageCols;
     static constexpr int kStagesBySmem = kSmemForStages / kStageBytes;

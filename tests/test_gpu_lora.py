@@ -123,12 +123,15 @@ def test_lora_rejects_bad_rank(ck):
 
 # ------------------------------------------------------------------ int8 operands (W8A8 tier, unpacked int4 codes)
 
+# 256 x 128 tiles (few tiles) and 256 x 256 tiles (at least one per SM), ragged edges
 @pytest.mark.parametrize("m,n,k,r", [(256, 256, 512, 64), (300, 1000, 1024, 16), (1024, 3072, 3072, 64),
-                                     (129, 264, 256, 8), (700, 3072, 12288, 64)])
+                                     (129, 264, 256, 8), (700, 3072, 12288, 64), (2304, 4096, 1024, 64),
+                                     (4608, 3072, 3072, 32), (2000, 3000, 2048, 64)])
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
 def test_int8_lora_on_unpacked_codes_equals_packed(ck, m, n, k, r, out_dtype):
-    """Same accumulators (sign-extended codes), same LoRA MMAs on the same 256 x 128
-    tiles, same epilogue: bit-identical to the packed kernel."""
+    """Same accumulators (sign-extended codes), same LoRA MMAs (a rank step of K = 16
+    per output element, whatever the tile width), same epilogue: bit-identical to the
+    packed kernel."""
     g = torch.Generator().manual_seed(m * 3 + n + r)
     xp = torch.randint(-128, 128, (m, k // 2), generator=g, dtype=torch.int8).cuda()
     wp = torch.randint(-128, 128, (n, k // 2), generator=g, dtype=torch.int8).cuda()
