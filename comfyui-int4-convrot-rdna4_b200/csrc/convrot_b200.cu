@@ -569,7 +569,9 @@ convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restric
         const int nrows = min(rows_per_round, M - row0);
         const bool active = my_row < nrows;
         uint32_t* rmax = rowmax + (it % 3) * kQ5MaxTiles;
-        const bool ok = mbar_wait_bounded(&full[buf], (it >> 1) & 1);
+        // one thread waits for the slab; the others sleep at the block barrier
+        // (no issue slots spent polling) and see the copy through it
+        const bool ok = !__syncthreads_or(tid == 0 && !mbar_wait_bounded(&full[buf], (it >> 1) & 1));
 
         uint32_t packed[8][8];                         // rounded rotated values, bf16 pairs
         // a tile's two halves are lanes l and l ^ 16: both in or both out
