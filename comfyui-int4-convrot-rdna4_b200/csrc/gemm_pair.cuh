@@ -53,11 +53,17 @@ constexpr uint32_t kEpiBarrier = 1;      // named barrier id of the epilogue war
 template <int BN, bool STAGED, bool SWAP, bool LORA = false, bool I8 = false>
 struct PairCfg {
     static constexpr int kBHalf = BN / 2;
-    static constexpr int kABytes = 128 * kPairBKP;
+    // int8 form with 256 x 128 tiles (few tiles: small M or N): two 128-byte K
+    // sub-tiles per stage, 8 MMAs per barrier wait and commit; a stage is
+    // [A sub 0 | A sub 1 | B sub 0 | B sub 1]. (256-column tiles keep one: their
+    // 64 KB double stages would leave a 3-deep ring.)
+    static constexpr int kSubK = (I8 && !STAGED && !LORA && BN <= 128) ? 2 : 1;
+    static constexpr int kStageK = kSubK * kPairBKP;               // operand bytes of K per stage
+    static constexpr int kABytes = 128 * kPairBKP;                 // one sub-tile
     static constexpr int kBBytes = kBHalf * kPairBKP;
-    static constexpr int kStageBytes = I8 ? kABytes + kBBytes : kABytes + 2 * kBBytes;
+    static constexpr int kStageBytes = I8 ? kSubK * (kABytes + kBBytes) : kABytes + 2 * kBBytes;
     static constexpr int kTmemStageCols = 2 * kPairBKP / 4;      // hi + lo bytes of a row, 4 per column
-    static constexpr int kMmasPerStage = (I8 ? 1 : 2) * kPairBKP / 32;   // K = 32 bytes per MMA
+    static constexpr int kMmasPerStage = (I8 ? kSubK : 2) * kPairBKP / 32;   // K = 32 bytes per MMA
     static constexpr int kAccShift = I8 ? 0 : 8;                  // int4 halves accumulate 256 * D
     // bf16 output tile staged for the TMA store: 128 rows x BN cols, 64-col boxes
     static constexpr int kStagingBytes = STAGED ? 128 * BN * 2 : 0;
@@ -198,7 +204,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
     const int cluster_id = blockIdx.x >> 1;
     const int num_clusters = gridDim.x >> 1;
     const int row_bytes = I8 ? K : (K >> 1);                       // operand bytes per row
-    const int num_kt = (row_bytes + kPairBKP - 1) / kPairBKP;
+    const int num_kt = (row_bytes + Cfg::kStageK - 1) / Cfg::kStageK;
     const int rows_a = SWAP ? N : M;
     // tiles of this cluster, and k-stage iterations over all of them
     const int my_tiles = (num_tiles - cluster_id + num_clusters - 1) / num_clusters;
@@ -236,10 +242,10 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         const int t = cluster_id;
         if constexpr (SWAP) {
             const int w_row0 = (t % tiles_a) * 256 + static_cast<int>(cta) * 128;
-            for (int kt = 0; kt < num_kt; ++kt) tma_prefetch_l2_2d(&tmap_a, kt * kPairBKP, w_row0);
+            for (int x = 0; x < num_kt * Cfg::kStageK; x += kPairBKP) tma_prefetch_l2_2d(&tmap_a, x, w_row0);
         } else {
             const int w_row0 = (t / tiles_a) * BN + static_cast<int>(cta) * Cfg::kBHalf;
-            for (int kt = 0; kt < num_kt; ++kt) tma_prefetch_l2_2d(&tmap_b, kt * kPairBKP, w_row0);
+            for (int x = 0; x < num_kt * Cfg::kStageK; x += kPairBKP) tma_prefetch_l2_2d(&tmap_b, x, w_row0);
         }
     };
     if (!I8 && warp == 0 && lane == 0) prefetch_first_weights();
@@ -286,9 +292,14 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                     if constexpr (I8) {
                         // both CTAs' tiles complete on the even CTA's barrier
                         const uint32_t full_leader = mapa_shared(smem_u32(&full_bar[s]), 0);
-                        if (cta == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * (Cfg::kABytes + Cfg::kBBytes));
-                        tma_load_2d_pair(st, &tmap_a, full_leader, kt * kPairBKP, a_row0);
-                        tma_load_2d_pair(st + Cfg::kABytes, &tmap_b, full_leader, kt * kPairBKP, b_row0);
+                        if (cta == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * Cfg::kStageBytes);
+                        #pragma unroll
+                        for (int sub = 0; sub < Cfg::kSubK; ++sub) {
+                            const int x = kt * Cfg::kStageK + sub * kPairBKP;
+                            tma_load_2d_pair(st + sub * Cfg::kABytes, &tmap_a, full_leader, x, a_row0);
+                            tma_load_2d_pair(st + Cfg::kSubK * Cfg::kABytes + sub * Cfg::kBBytes, &tmap_b,
+                                             full_leader, x, b_row0);
+                        }
                     } else {
                         mbar_arrive_expect_tx(&full_bar[s], Cfg::kABytes + Cfg::kBBytes);
                         tma_load_2d(st, &tmap_a, &full_bar[s], kt * kPairBKP, a_row0);
@@ -322,13 +333,20 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                     }
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(smem + s * Cfg::kStageBytes);
-                    // K-major, 128 B swizzle: the j-th 32-byte K step is +2 in the address field
-                    const uint64_t da = smem_desc_kmajor(a_addr, 8 * kPairBKP, kSwizzle128);
-                    const uint64_t db = smem_desc_kmajor(a_addr + Cfg::kABytes, 8 * kPairBKP, kSwizzle128);
+                    const uint32_t b_addr = a_addr + Cfg::kSubK * Cfg::kABytes;
+                    // K-major, 128 B swizzle: the j-th 32-byte K step of a sub-tile is +2
+                    // in the address field
+                    uint64_t da[Cfg::kSubK], db[Cfg::kSubK];
+                    #pragma unroll
+                    for (int sub = 0; sub < Cfg::kSubK; ++sub) {
+                        da[sub] = smem_desc_kmajor(a_addr + sub * Cfg::kABytes, 8 * kPairBKP, kSwizzle128);
+                        db[sub] = smem_desc_kmajor(b_addr + sub * Cfg::kBBytes, 8 * kPairBKP, kSwizzle128);
+                    }
                     if (elect_one()) {
                         #pragma unroll
                         for (int j = 0; j < Cfg::kMmasPerStage; ++j)
-                            mma_i8_ss_pair(acc_tmem, da + 2 * j, db + 2 * j, Cfg::kIdesc, (kt | j) != 0);
+                            mma_i8_ss_pair(acc_tmem, da[j >> 2] + 2 * (j & 3), db[j >> 2] + 2 * (j & 3),
+                                           Cfg::kIdesc, (kt | j) != 0);
                         mma_commit_pair_multicast(&empty_bar[s], 0x3);
                     }
                     __syncwarp();
