@@ -45,8 +45,22 @@ __all__ = [
 # Output dtypes the GEMM epilogue writes directly; others compute f32 then cast.
 _NATIVE_OUT = frozenset({torch.float32, torch.bfloat16})
 # Rows from which a layer runs on unpacked codes (int8 pipeline); fewer tokens
-# keep the packed paths, which read each weight once as int4.
+# keep the packed paths, which read each weight once as int4 -- except layers
+# with few output rows (N <= _FEW_ROWS_N: a dozen swapped 256-row tiles leave
+# most SMs idle), which run unpacked once M * K >= _FEW_ROWS_MIN_MK (measured on
+# 3072 x 3072 .. 12288 x 4096 weights; below it, and under 5 tokens where the
+# few-token GEMV streams the packed weights, the packed paths are as fast).
 _UNPACKED_MIN_ROWS = 129
+_FEW_ROWS_N = 4096
+_FEW_ROWS_MIN_MK = 8 * 12288
+
+
+def _use_unpacked(x2d: torch.Tensor, qweight: torch.Tensor, convrot_groupsize: int) -> bool:
+    m, k = x2d.shape
+    few_rows = qweight.shape[0] <= _FEW_ROWS_N and m >= 5 and m * k >= _FEW_ROWS_MIN_MK
+    if m < _UNPACKED_MIN_ROWS and not few_rows:
+        return False
+    return weight_cache.enabled() and cuda_loader.unpacked_path_supported(x2d, convrot_groupsize)
 
 
 def set_unpacked_weights(enabled: bool = True) -> None:
@@ -108,8 +122,7 @@ def convrot_w4a4_linear(
     shape = x.shape
     x2d = x.reshape(-1, shape[-1]).contiguous()
     out_dtype = x.dtype if x.dtype in _NATIVE_OUT else torch.float32
-    if (weight_cache.enabled() and x2d.shape[0] >= _UNPACKED_MIN_ROWS
-            and cuda_loader.unpacked_path_supported(x2d, convrot_groupsize)):
+    if _use_unpacked(x2d, qweight, convrot_groupsize):
         # many tokens: both operands as int8 codes on the int8 tensor-core pipeline
         # (same accumulators, same results); the weight's codes are cached
         codes = weight_cache.unpacked(qweight)
@@ -149,8 +162,7 @@ def convrot_w4a4_linear_lora(
     x2d = x.reshape(-1, shape[-1]).contiguous()
     lora_t, up, scale = _lora_operands(x2d, adapters, qweight.shape[0])
     out_dtype = x.dtype if x.dtype in _NATIVE_OUT else torch.float32
-    if (weight_cache.enabled() and x2d.shape[0] >= _UNPACKED_MIN_ROWS
-            and cuda_loader.unpacked_path_supported(x2d, convrot_groupsize)):
+    if _use_unpacked(x2d, qweight, convrot_groupsize):
         qact, x_scale = cuda_loader.convrot_quant_int4_unpacked(x2d, convrot_groupsize)
         out = cuda_loader.int8_convrot_gemm_lora(qact, weight_cache.unpacked(qweight), x_scale, wscales, bias,
                                                  out_dtype, lora_t, up, scale)

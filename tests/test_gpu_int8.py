@@ -197,3 +197,25 @@ def test_public_linear_takes_unpacked_path_for_many_tokens(ck):
     assert torch.equal(y, y_packed)
     ora = orc.convrot_w4a4_linear(bits(x), qw.cpu().numpy(), ws.cpu().numpy(), None, 256)
     assert np.array_equal(bits(y), ora)
+
+
+@pytest.mark.parametrize("m,k,n,unpacked", [(64, 12288, 3072, True), (32, 3072, 3072, True),
+                                           (16, 3072, 3072, False), (64, 3072, 12288, False),
+                                           (4, 3072, 3072, False)])
+def test_public_linear_few_rows_dispatch(ck, m, k, n, unpacked):
+    """5..128 tokens: few-row layers (N <= 4096, M * K >= 8 * 12288) take the unpacked
+    path, others stay packed; the output bits are the packed path's either way."""
+    import _int4
+    from _int4 import weight_cache
+    weight_cache.enable(True)
+    x = activation(m, k, m + n)
+    w = (torch.randn(n, k) * 0.02).to(torch.float16).cuda()
+    qw, ws = _int4.quantize_convrot_w4a4_weight(w, 256)
+    before = weight_cache.cached_bytes()
+    y = _int4.convrot_w4a4_linear(x, qw, ws)
+    assert weight_cache.cached_bytes() == before + (n * k if unpacked else 0)
+    weight_cache.enable(False)
+    y_packed = _int4.convrot_w4a4_linear(x, qw, ws)
+    weight_cache.enable(True)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y_packed)

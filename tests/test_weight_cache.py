@@ -49,3 +49,21 @@ def test_disable_frees_everything():
     weight_cache.enable(False)
     assert weight_cache.cached_bytes() == 0 and not weight_cache.enabled()
     weight_cache.enable(True)
+
+
+def test_unpacked_dispatch_rule(monkeypatch):
+    import _int4
+    from _int4 import cuda_loader
+    monkeypatch.setattr(cuda_loader, "unpacked_path_supported", lambda x, g: True)
+    weight_cache.enable(True)
+
+    def use(m, n, k=3072):
+        return _int4._use_unpacked(torch.zeros(m, k), torch.zeros(n, k // 2, dtype=torch.int8), 256)
+    assert use(129, 18432) and use(4608, 3072)                 # many tokens
+    assert use(32, 3072) and use(8, 4096, 12288)               # few rows: a dozen swapped tiles
+    assert not use(16, 3072) and not use(7, 3072, 12288)       # too little work per weight byte
+    assert not use(64, 12288) and not use(128, 4352)           # enough swapped tiles: packed
+    assert not use(4, 3072, 65536) and not use(1, 3072)        # few-token GEMV
+    weight_cache.enable(False)
+    assert not use(4608, 3072)
+    weight_cache.enable(True)
