@@ -42,6 +42,7 @@ _SIGNATURES = {
     "ck_convrot_w4a4_linear_unpacked_workspace_size": [_I, _I],
     "ck_convrot_w4a4_linear_unpacked": [_P, _I, _P, _P, _P, _I, _P] + [_I] * 5 + [_P, ctypes.c_size_t, _P],
     "ck_convrot_device_status": [_P, ctypes.POINTER(ctypes.c_int)],
+    "ck_convrot_selftest_wait_timeout": [ctypes.c_longlong, _P],
     "ck_convrot_last_error": [],
 }
 
@@ -285,6 +286,14 @@ def int4_gemm_s32(x_packed, w_packed):
                               _stream(x_packed))
     _check("ck_int4_gemm_s32", rc)
     return acc
+
+
+def selftest_wait_timeout(limit_ns: int, device=None) -> None:
+    """Launch the failure-path self test (a bounded wait nothing ends); afterwards
+    device_status() returns 5."""
+    lib = _load()
+    stream = torch.cuda.current_stream(device).cuda_stream
+    _check("ck_convrot_selftest_wait_timeout", lib.ck_convrot_selftest_wait_timeout(int(limit_ns), stream))
 
 
 def device_status(device=None) -> int:

@@ -52,6 +52,7 @@ enum : int {
     kStatusTimeoutMma = 2,
     kStatusTimeoutExpand = 3,
     kStatusTimeoutEpilogue = 4,
+    kStatusTimeoutSelfTest = 5,
 };
 
 __device__ __forceinline__ void record_status(int code) { atomicCAS(&g_device_status, 0, code); }
@@ -1675,6 +1676,24 @@ CONVROT_API int ck_convrot_w4a4_linear_unpacked(const void* x, int in_dtype, con
     const float* ws = static_cast<const float*>(wscale);
     if (out_dtype == 1) return dispatch_gemm_i8<kOutBF16>(q, Wcodes, xs, ws, b, out, M, N, K, s);
     return dispatch_gemm_i8<kOutF32>(q, Wcodes, xs, ws, b, out, M, N, K, s);
+}
+
+// A wait that nothing ends: one thread waits on a fresh mbarrier that no one
+// arrives on, gives up after limit_ns, records kStatusTimeoutSelfTest and
+// returns -- the path every pipeline wait takes when a partner never shows up.
+__global__ void selftest_wait_timeout_kernel(unsigned long long limit_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    if (!mbar_wait_bounded(&bar, 0, limit_ns)) record_status(kStatusTimeoutSelfTest);
+}
+
+CONVROT_API int ck_convrot_selftest_wait_timeout(long long limit_ns, void* stream) {
+    if (limit_ns <= 0 || limit_ns > 100000000LL) return fail("limit_ns must be in (0, 1e8]");
+    selftest_wait_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<unsigned long long>(limit_ns));
+    return static_cast<int>(cudaGetLastError());
 }
 
 CONVROT_API int ck_convrot_device_status(void* stream, int* status) {

@@ -192,6 +192,13 @@ int ck_convrot_w4a4_linear_unpacked(const void* x, int in_dtype, const void* Wco
  * the reference has no device-side timeouts. */
 int ck_convrot_device_status(void* stream, int* status);
 
+/* Failure-path self test: launches one thread that waits on an mbarrier nothing
+ * arrives on, with the bounded wait every pipeline wait uses, cut to limit_ns
+ * (0 < limit_ns <= 1e8). It gives up, records status 5 (read and cleared by
+ * ck_convrot_device_status) and returns, leaving the context usable. No
+ * reference counterpart: it exercises the timeout path without faulting a GPU. */
+int ck_convrot_selftest_wait_timeout(long long limit_ns, void* stream);
+
 /* Human-readable reason for the last -1 returned on this host thread. */
 const char* ck_convrot_last_error(void);
 

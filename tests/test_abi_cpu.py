@@ -111,6 +111,12 @@ def test_linear_rejects_bad_arguments(lib):
     assert call(m=0) == 0 and call(n=0) == 0                  # empty: nothing launched
 
 
+def test_selftest_wait_rejects_bad_limit(lib):
+    assert lib.ck_convrot_selftest_wait_timeout(0, None) == -1
+    assert lib.ck_convrot_selftest_wait_timeout(200_000_000, None) == -1
+    assert b"limit_ns" in lib.ck_convrot_last_error()
+
+
 def test_int8_lora_rejects_bad_arguments(lib):
     f = lib.ck_int8_convrot_gemm_lora
     assert f(16, 16, 16, 16, 0, 0, 16, 256, 256, 256, 1, 16, 16, 12, 1.0, None) == -1   # rank not a multiple of 8
