@@ -468,7 +468,7 @@ def run_ours(args, rank, world, local_rank):
         # time the kernels the public linear runs for this layer: with the
         # unpacked-weight cache on (default) and M > 128 that is the int8 pair GEMM
         # on sign-extended codes, else the int4 pair GEMM on packed codes
-        unpacked = weight_cache.enabled() and m >= _int4._UNPACKED_MIN_ROWS
+        unpacked = _int4._use_unpacked(xs[(m, k)], up["qw"], GROUP)
         if unpacked:
             quant = ck.convrot_quant_int4_unpacked
             wq = weight_cache.unpacked(up["qw"])
