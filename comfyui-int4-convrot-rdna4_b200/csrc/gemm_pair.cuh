@@ -323,7 +323,28 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                 }
                 const uint32_t acc_tmem = tmem_base + abuf * Cfg::kAccCols;
                 tc_fence_after();
-                for (int kt = 0; kt < num_kt; ++kt, ++it) {
+                if constexpr (LORA) {
+                    // the side path T . B^T on bf16 MMAs into this buffer's fp32 half, ahead
+                    // of the K loop: its operand slot is then free for the next tile's
+                    // side path early, and the producer does not stall between tiles
+                    if (ok && !__all_sync(0xFFFFFFFFu, mbar_wait_bounded(lora_full_bar, lt & 1))) {
+                        if (lane == 0) record_status(kStatusTimeoutMma);
+                        ok = false;
+                    }
+                    if (ok) {
+                        tc_fence_after();
+                        const uint64_t dt = smem_desc_kmajor(smem_u32(lora_t), 1024, kSwizzle128);
+                        const uint64_t dl = smem_desc_kmajor(smem_u32(lora_b), 1024, kSwizzle128);
+                        if (elect_one()) {
+                            #pragma unroll
+                            for (int j = 0; j < 4; ++j)    // rank 64 = four K = 16 bf16 steps of a 128 B row
+                                mma_bf16_ss_pair(tmem_lora(abuf), dt + 2 * j, dl + 2 * j, Cfg::kIdescLora, j != 0);
+                            mma_commit_pair_multicast(lora_empty_bar, 0x3);
+                        }
+                        __syncwarp();
+                    }
+                }
+                for (int kt = 0; kt < num_kt && ok; ++kt, ++it) {
                     const int s = it % Cfg::kStages;
                     const uint32_t ph = (it / Cfg::kStages) & 1;
                     if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(&full_bar[s], ph))) {
@@ -351,25 +372,6 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                     }
                     __syncwarp();
                 }
-                if constexpr (LORA) {
-                    // the side path T . B^T on bf16 MMAs into this buffer's fp32 half
-                    if (ok && !__all_sync(0xFFFFFFFFu, mbar_wait_bounded(lora_full_bar, lt & 1))) {
-                        if (lane == 0) record_status(kStatusTimeoutMma);
-                        ok = false;
-                    }
-                    if (ok) {
-                        tc_fence_after();
-                        const uint64_t dt = smem_desc_kmajor(smem_u32(lora_t), 1024, kSwizzle128);
-                        const uint64_t dl = smem_desc_kmajor(smem_u32(lora_b), 1024, kSwizzle128);
-                        if (elect_one()) {
-                            #pragma unroll
-                            for (int j = 0; j < 4; ++j)    // rank 64 = four K = 16 bf16 steps of a 128 B row
-                                mma_bf16_ss_pair(tmem_lora(abuf), dt + 2 * j, dl + 2 * j, Cfg::kIdescLora, j != 0);
-                            mma_commit_pair_multicast(lora_empty_bar, 0x3);
-                        }
-                        __syncwarp();
-                    }
-                }
                 if (ok && elect_one()) mma_commit_pair_multicast(&acc_full_bar[abuf], 0x3);
                 __syncwarp();
             }
@@ -387,7 +389,22 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                 }
                 const uint32_t acc_tmem = tmem_base + abuf * Cfg::kAccCols;
                 tc_fence_after();
-                for (int kt = 0; kt < num_kt; ++kt, ++it) {
+                if constexpr (LORA) {
+                    if (ok && !mbar_wait_bounded<true>(lora_full_bar, lt & 1)) {
+                        record_status(kStatusTimeoutMma); ok = false;
+                    }
+                    if (ok) {                              // side path first (see the int8 issuer)
+                        tc_fence_after();
+                        const uint32_t t_addr = smem_u32(lora_t), b_addr = smem_u32(lora_b);
+                        #pragma unroll
+                        for (int j = 0; j < 4; ++j)        // rank 64 = four K = 16 bf16 steps of a 128 B row
+                            mma_bf16_ss_pair(tmem_lora(abuf), smem_desc_kmajor(t_addr + 32 * j, 1024, kSwizzle128),
+                                             smem_desc_kmajor(b_addr + 32 * j, 1024, kSwizzle128),
+                                             Cfg::kIdescLora, j != 0);
+                        mma_commit_pair_multicast(lora_empty_bar, 0x3);
+                    }
+                }
+                for (int kt = 0; kt < num_kt && ok; ++kt, ++it) {
                     const int s = it % Cfg::kStages;
                     const uint32_t ph = (it / Cfg::kStages) & 1;
                     if (!mbar_wait_bounded<true>(&ready_bar[s], ph)) {
@@ -405,21 +422,6 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                     }
                     mma_commit_pair_multicast(&empty_bar[s], 0x3);
                     mma_commit_pair_multicast(&tmem_free_bar[ts], 0x3);
-                }
-                if constexpr (LORA) {
-                    if (ok && !mbar_wait_bounded<true>(lora_full_bar, lt & 1)) {
-                        record_status(kStatusTimeoutMma); ok = false;
-                    }
-                    if (ok) {
-                        tc_fence_after();
-                        const uint32_t t_addr = smem_u32(lora_t), b_addr = smem_u32(lora_b);
-                        #pragma unroll
-                        for (int j = 0; j < 4; ++j)        // rank 64 = four K = 16 bf16 steps of a 128 B row
-                            mma_bf16_ss_pair(tmem_lora(abuf), smem_desc_kmajor(t_addr + 32 * j, 1024, kSwizzle128),
-                                             smem_desc_kmajor(b_addr + 32 * j, 1024, kSwizzle128),
-                                             Cfg::kIdescLora, j != 0);
-                        mma_commit_pair_multicast(lora_empty_bar, 0x3);
-                    }
                 }
                 if (ok) mma_commit_pair_multicast(&acc_full_bar[abuf], 0x3);
             }
