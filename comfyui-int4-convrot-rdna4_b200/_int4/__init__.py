@@ -135,6 +135,9 @@ def convrot_w4a4_linear(
 
 
 _MAX_LORA_RANK = 64
+# Unit roundoff of the side path's operand type (T = x.A^T and B enter the
+# tensor cores in bf16): the bound a caller's tolerance on the LoRA term needs.
+LORA_OPERAND_UNIT = 2.0 ** -8
 
 
 def convrot_w4a4_linear_lora(

@@ -1,13 +1,15 @@
 """Torch ConvRot W8A8 helpers (the int8 middle tier of mixed precision).
 
 Same rotation as int4; plain int8 storage [N, K] and scale = absmax / 127
-(reference: _int4/int8_eager.py:19-89).
+(reference: _int4/int8_eager.py:19-57). These define the bytes of int8 layers
+and of the activation codes where the fused kernel does not apply; the W8A8
+forward itself is ``_int4.convrot_w8a8_linear`` (CUDA kernels only).
 """
 from __future__ import annotations
 
 import torch
 
-from .eager import _build_hadamard, _rotate_activation, _rotate_weight
+from .eager import _build_hadamard, _rotate_weight
 
 _INT8_MAX = 127
 
@@ -35,20 +37,3 @@ def dequantize_convrot_w8a8_weight(qdata: torch.Tensor, scales: torch.Tensor, co
     h = _build_hadamard(convrot_groupsize, device=qdata.device, dtype=torch.float32)
     return _rotate_weight(w, h, convrot_groupsize).to(output_dtype)
 
-
-def convrot_w8a8_linear(x: torch.Tensor, qweight: torch.Tensor, wscales: torch.Tensor,
-                        bias: torch.Tensor | None = None, convrot_groupsize: int = 256) -> torch.Tensor:
-    """x @ W^T + bias with on-the-fly int8 activation quantization (torch ops)."""
-    if x.shape[-1] != qweight.shape[-1]:
-        raise ValueError(f"Input K={x.shape[-1]} does not match qweight K={qweight.shape[-1]}")
-    if x.shape[-1] % convrot_groupsize:
-        raise ValueError(f"Input K={x.shape[-1]} not divisible by convrot_groupsize {convrot_groupsize}")
-    shape = x.shape
-    x2d = x.reshape(-1, shape[-1]).contiguous()
-    h = _build_hadamard(convrot_groupsize, device=x2d.device, dtype=x2d.dtype)
-    q, xs = quantize_signed_int8_rowwise(_rotate_activation(x2d, h, convrot_groupsize).contiguous())
-    out = q.to(torch.float32) @ qweight.to(torch.float32).t()
-    out = out * xs.reshape(-1, 1) * wscales.to(out.device, torch.float32).reshape(1, -1)
-    if bias is not None:
-        out = out + bias.to(out.device, torch.float32).reshape(1, -1)
-    return out.to(x.dtype).reshape(*shape[:-1], qweight.shape[0])

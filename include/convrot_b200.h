@@ -78,11 +78,14 @@ int ck_convrot_w4a4_linear(const void* x, int in_dtype, const void* Wp, const vo
                            int M, int N, int K, int G, void* workspace, size_t workspace_bytes,
                            void* stream);
 
-/* ck_convrot_w4a4_linear for callers that cannot allocate device memory: the
- * same arguments minus the workspace, which is replaced by a static 128 MiB
- * device array per device (placed when the library's no-alloc module loads;
- * the entry itself allocates nothing). No reference counterpart: the
- * reference always allocates its intermediates with torch.
+/* ck_convrot_w4a4_linear for callers that cannot allocate device memory (a
+ * host framework that owns every device buffer through its own arena and only
+ * hands this library inputs and outputs, a plugin ABI with plain pointers and
+ * no allocator): the same arguments minus the workspace, which is replaced by
+ * a static 128 MiB device array per device, placed when the library's no-alloc
+ * module loads on that device. The entry itself allocates nothing. No
+ * reference counterpart: the reference always allocates its intermediates
+ * with torch.
  *   - limit: ck_convrot_w4a4_linear_workspace_size(M, K) <= 134217728 bytes
  *     (e.g. M = 18432 rows at K = 12288); larger sizes return -1 before any
  *     CUDA call, with the reason in ck_convrot_last_error();
@@ -91,7 +94,11 @@ int ck_convrot_w4a4_linear(const void* x, int in_dtype, const void* Wp, const vo
  *   - one scratch per device: calls that may overlap in time (other streams,
  *     other host threads) race on it; calls on one stream are ordered and safe;
  *   - the first call on each device does the setup (a cudaGetSymbolAddress
- *     with that device current): make it before capturing a CUDA graph. */
+ *     with that device current), and so does the first call after that
+ *     device's primary context was reset: make it before any stream capture;
+ *   - with lazy module loading (the default) only processes that call this
+ *     entry hold the 128 MiB; with CUDA_MODULE_LOADING=EAGER every process
+ *     that loads the library holds it on each device it uses. */
 int ck_convrot_w4a4_linear_noalloc(const void* x, int in_dtype, const void* Wp, const void* wscale,
                                    const void* bias, int bias_dtype, void* out, int out_dtype,
                                    int M, int N, int K, int G, void* stream);

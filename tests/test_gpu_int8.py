@@ -9,6 +9,7 @@ import pytest
 import torch
 
 from oracle import convrot_oracle as orc
+from oracle import eager_torch
 
 pytestmark = pytest.mark.gpu
 GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
@@ -139,7 +140,7 @@ def test_w8a8_linear_other_shapes_take_torch_quant_then_native_gemm(ck):
     from _int4 import int8_eager
     qw, ws = int8_eager.quantize_convrot_w8a8_weight(w, 256)
     out = _int4.convrot_w8a8_linear(x, qw, ws)
-    ref = int8_eager.convrot_w8a8_linear(x, qw, ws)
+    ref = eager_torch.convrot_w8a8_linear(x, qw, ws)
     torch.cuda.synchronize()
     assert out.dtype == torch.float16
     rel = (out.float() - ref.float()).norm() / ref.float().norm()

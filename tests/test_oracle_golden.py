@@ -233,3 +233,32 @@ def test_int8_weight_quant_torch_matches_reference_bytes(case):
     qw, ws = int8_eager.quantize_convrot_w8a8_weight(w, grp)
     assert np.array_equal(qw.numpy(), g[f"l_{case}_qw"])
     assert np.array_equal(ws.numpy().view(np.uint32), g[f"l_{case}_ws"].view(np.uint32))
+
+
+def _bf16(a):
+    import torch
+    return torch.from_numpy(a.view(np.int16).copy()).view(torch.bfloat16)
+
+
+@pytest.mark.parametrize("case", LIN_CASES)
+def test_eager_torch_port_matches_reference_linear_bits(case):
+    """oracle.eager_torch (the CPU baseline's fallback) reproduces the reference's
+    eager W4A4 linear bit for bit on the CPU."""
+    from oracle import eager_torch
+    lin = load("linear.npz")
+    grp = int(lin[f"{case}_meta"][0])
+    import torch
+    out = eager_torch.convrot_w4a4_linear(_bf16(lin[f"{case}_x"]), torch.from_numpy(lin[f"{case}_qw"]),
+                                          torch.from_numpy(lin[f"{case}_ws"]), _bf16(lin[f"{case}_bias"]), grp)
+    assert np.array_equal(out.view(torch.int16).numpy().view(np.uint16), lin[f"{case}_out"])
+
+
+@pytest.mark.parametrize("case", ["g256", "g64", "cfg0"])
+def test_eager_torch_port_matches_reference_w8a8_linear_bits(case):
+    from oracle import eager_torch
+    import torch
+    g = load("int8.npz")
+    grp = int(g[f"l_{case}_meta"][0])
+    out = eager_torch.convrot_w8a8_linear(_bf16(g[f"l_{case}_x"]), torch.from_numpy(g[f"l_{case}_qw"]),
+                                          torch.from_numpy(g[f"l_{case}_ws"]), _bf16(g[f"l_{case}_bias"]), grp)
+    assert np.array_equal(out.view(torch.int16).numpy().view(np.uint16), g[f"l_{case}_out"])
