@@ -2,19 +2,27 @@
 
 One step = the Flux-class double-block linear set at M = 4608 tokens:
 QKV 3072->9216, attention-out 3072->3072, MLP-up 3072->12288 and MLP-down
-12288->3072, each a full W4A4 forward (fused rotate+quantize kernel, then the
-tcgen05 int4 GEMM with the dequant + bias epilogue). Metric: W4A4 linear TOPS
-(2*M*N*K ops per layer; integer MACs count as two ops).
+12288->3072, each a full W4A4 forward through the public API
+(``_int4.convrot_w4a4_linear``: fused rotate+quantize kernel, then the tcgen05
+GEMM with the dequant + bias epilogue). Metric: W4A4 linear TOPS (2*M*N*K ops
+per layer; integer MACs count as two ops).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-N > 1 runs under torchrun, one process per GPU: token-parallel replicas (each
-rank runs its own 4608-token step with replicated weights, no collective on
-the data path), weak scaling; the step time is the max over ranks.
+N > 1 runs under torchrun, one process per GPU: the step's 4608 tokens are
+split over the ranks (4608/N rows each, weights replicated, no collective on
+the data path), strong scaling; the step time is the max over ranks. Extra
+keys of the same line: ``replicas`` (every rank runs all 4608 tokens: weak
+scaling), ``nsplit`` (config 4's 12288->3072 layer with its LoRA side path,
+split by output columns over the ranks and gathered over NVLink), and at
+N = 1 ``dit_step`` (one denoising step of a synthetic Flux-architecture DiT,
+config 2) plus the per-kernel roofline probes.
 
-``--impl reference`` times the CPU restatement of the reference algorithm
-(oracle/convrot_oracle.py, the port of _int4/eager.py + the HIP epilogue) on
-the host cores, rank 0 only.
+``--impl reference`` times the reference's own CPU implementation of the path,
+``_int4.eager.convrot_w4a4_linear`` imported from ``baseline/_ref`` (installed
+by ``oracle/ref_install.py``; its torch restatement ``oracle/eager_torch.py``
+when that is absent), on every host core, rank 0 only, on the same 4608-token
+step.
 
 Timing: inputs are resident in HBM; L2 is flushed (a 256 MiB write) before
 every timed step; each step is bracketed by CUDA events on the launching
@@ -24,6 +32,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -45,13 +54,15 @@ HIDDEN = 3072
 LAYERS = [("qkv", 3072, 9216), ("attn_out", 3072, 3072), ("mlp_up", 3072, 12288), ("mlp_down", 12288, 3072)]
 GROUP = 256
 LORA_RANK = 64
+REF_BUDGET_S = 150.0          # bound on the reference arm's whole --steps/--warmup run
+
 
 def flux_dit_layers():
     """Every int4 Linear of one forward of a Flux-architecture DiT (config 2): 19 double
     blocks (image stream at 4096 tokens, text stream at 512) and 38 single blocks at
-    4608 tokens, hidden 3072, MLP x4; the modulation Linears run at M = 1. The
-    embedders and the final layer stay bf16 in the reference loader (EXCLUDED list)."""
-    layers = []
+    4608 tokens, hidden 3072, MLP x4; the modulation Linears and vector_in run at M = 1.
+    The embedders and the final layer stay bf16 (the reference loader's skip list)."""
+    layers = [("vector_in.in_layer", 1, 768, 3072, 0), ("vector_in.out_layer", 1, 3072, 3072, 0)]
     for d in range(19):
         for stream, m in (("img", 4096), ("txt", 512)):
             layers += [(f"d{d}.{stream}_attn.qkv", m, 3072, 9216, 0), (f"d{d}.{stream}_attn.proj", m, 3072, 3072, 0),
@@ -89,7 +100,12 @@ def layer_ops(m, k, n, r) -> int:
     return 2 * m * n * k + (2 * m * r * (k + n) if r else 0)
 
 
-def workload_config(cfg_id=1, extra=None):
+def shard_range(m: int, rank: int, world: int):
+    """Rows [lo, hi) of m tokens that `rank` of `world` runs (token split)."""
+    return rank * m // world, (rank + 1) * m // world
+
+
+def workload_config(cfg_id=1, world=1, extra=None):
     name, layers = WORKLOADS[cfg_id]
     if cfg_id == 2:
         shapes = sorted({(m, k, n) for _, m, k, n, _ in layers}, reverse=True)
@@ -98,10 +114,14 @@ def workload_config(cfg_id=1, extra=None):
                 "weights": "random packed int4 codes and scales (the kernels' work does not depend on the values)"}
     else:
         desc = {"layers": {lname: f"M={m} {k}->{n}" + (f" +LoRA r={r}" if r else "") for lname, m, k, n, r in layers}}
-    cfg = {"workload": name, **desc,
-           "convrot_groupsize": GROUP, "l2": "flushed before every timed step (256 MiB write)"}
+    cfg = {"workload": name, **desc, "convrot_groupsize": GROUP,
+           "l2": "flushed before every timed step (256 MiB write)"}
+    if cfg_id == 2 or world == 1:
+        cfg["parallelism"] = "single GPU"
+    else:
+        cfg["parallelism"] = f"token split x{world}: each rank runs 1/{world} of every layer's rows, weights replicated"
     if cfg_id == 1:
-        cfg.update({"tokens_per_gpu": M_TOKENS, "hidden": HIDDEN})
+        cfg.update({"tokens": M_TOKENS, "tokens_per_gpu": M_TOKENS // world, "hidden": HIDDEN})
     if extra:
         cfg.update(extra)
     return cfg
@@ -113,15 +133,6 @@ def load_peaks():
         with open(path) as f:
             return json.load(f), "measured"
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
-
-
-def load_traffic():
-    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "roofline_traffic.json")
-    if not os.path.exists(path):
-        return None
-    with open(path) as f:
-        return json.load(f)
 
 
 def synth_activation(m, k, gen, device):
@@ -199,72 +210,98 @@ class ClockSampler:
 
 # --------------------------------------------------------------------------- CPU arm
 
-class CpuWorkload:
-    """The oracle port of the reference path (all four layers) on `rows` tokens."""
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
-    def __init__(self, rows: int, seed: int = 0):
-        from oracle import convrot_oracle as orc
-        self.orc = orc
-        self.rows = rows
-        rng = np.random.default_rng(seed)
+
+def reference_impl():
+    """The reference's own CPU implementation of the path: (weight quantizer, linear,
+    kind, description). The reference package from baseline/_ref when installed,
+    else the torch restatement of the same eager code (bit-identical on the CPU)."""
+    root = os.path.join(ROOT, "baseline", "_ref", "_int4")
+    if os.path.exists(os.path.join(root, "eager.py")):
+        import importlib.util
+        spec = importlib.util.spec_from_file_location("convrot_reference_int4", os.path.join(root, "__init__.py"),
+                                                      submodule_search_locations=[root])
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[spec.name] = mod
+        spec.loader.exec_module(mod)
+        return (mod.quantize_convrot_w4a4_weight, mod.eager.convrot_w4a4_linear, "reference",
+                "the reference's _int4.eager.convrot_w4a4_linear (baseline/_ref), torch CPU")
+    from _int4.eager import quantize_convrot_w4a4_weight
+    from oracle import eager_torch
+    return (quantize_convrot_w4a4_weight, eager_torch.convrot_w4a4_linear, "port",
+            "oracle/eager_torch.convrot_w4a4_linear (torch restatement of _int4/eager.py:172-197), torch CPU")
+
+
+class CpuWorkload:
+    """Config 1's four layers on the host through `linear`, inputs built once."""
+
+    def __init__(self, quant_weight, linear, seed: int = 0):
+        self.linear = linear
+        gen = torch.Generator().manual_seed(seed)
         self.layers = []
         for _, k, n in LAYERS:
-            w = (rng.standard_normal((n, k), dtype=np.float32) * 0.02).astype(np.float16)
-            wp, ws = orc.quantize_weight(w, GROUP, "f16")
-            bias = (rng.standard_normal(n, dtype=np.float32) * 0.01).astype(np.float16).astype(np.float32)
-            x = rng.standard_normal((rows, k), dtype=np.float32)
-            x[:, rng.permutation(k)[: k // 100]] *= 20
-            # weights stay decoded across steps, like resident device weights
-            self.layers.append((orc.f32_to_bf16_bits(x), orc.decode_weight(wp), ws, bias))
+            w = (torch.randn(n, k, generator=gen) * 0.02).to(torch.float16)
+            qw, ws = quant_weight(w, GROUP)
+            bias = (torch.randn(n, generator=gen) * 0.01).to(torch.bfloat16).to(torch.float16)
+            self.layers.append((synth_activation(M_TOKENS, k, gen, "cpu"), qw, ws, bias))
 
-    def step(self) -> float:
+    def step(self, rows: int = M_TOKENS) -> float:
         t0 = time.perf_counter()
-        for x, wcodes, ws, bias in self.layers:
-            self.orc.convrot_w4a4_linear_decoded(x, wcodes, ws, bias, GROUP)
+        for x, qw, ws, bias in self.layers:
+            self.linear(x[:rows], qw, ws, bias, GROUP)
         return time.perf_counter() - t0
 
 
-def cpu_sample(rows: int, budget_s: float, seed: int = 0):
-    """Median step time of the oracle port over about `budget_s` seconds: (TOPS, s, steps)."""
-    wl = CpuWorkload(rows, seed)
+def cpu_sample(budget_s: float):
+    """CPU baseline of the default run: full 4608-token steps through the reference's
+    CPU path for about `budget_s` seconds (at least 3), median."""
+    quant_weight, linear, kind, what = reference_impl()
+    torch.set_num_threads(host_cores())
+    wl = CpuWorkload(quant_weight, linear)
     wl.step()
     times = []
     t_end = time.perf_counter() + budget_s
-    while len(times) < 2 or time.perf_counter() < t_end:
+    while len(times) < 3 or time.perf_counter() < t_end:
         times.append(wl.step())
     t = statistics.median(times)
-    return step_ops(rows) / t / 1e12, t, len(times)
+    return {"value": step_ops(M_TOKENS) / t / 1e12, "unit": UNIT, "cores": torch.get_num_threads(), "kind": kind,
+            "ms_per_step": t * 1e3,
+            "sample": f"all {M_TOKENS} tokens through the four layers, median of {len(times)} steps: {what}"}
 
 
-def cpu_threads():
-    try:
-        from threadpoolctl import threadpool_info
-        n = [i.get("num_threads") for i in threadpool_info() if i.get("user_api") == "blas"]
-        if n:
-            return int(max(n))
-    except Exception:
-        pass
-    return os.cpu_count() or 1
-
-
-def run_reference(args, rank):
+def run_reference(args, rank, world):
     if rank != 0:
         return
-    rows = args.cpu_rows
-    wl = CpuWorkload(rows)
-    for _ in range(args.warmup):
-        wl.step()
-    times = [wl.step() for _ in range(args.steps)]
-    t = statistics.median(times)
+    quant_weight, linear, kind, what = reference_impl()
+    torch.set_num_threads(host_cores())
+    wl = CpuWorkload(quant_weight, linear)
+    t_first = wl.step()                              # first warm-up step, also sizes the sample
+    rows = M_TOKENS
+    runs = args.steps + args.warmup - 1
+    if t_first * runs > REF_BUDGET_S:                # keep the whole run within a few minutes
+        rows = max(256, int(M_TOKENS * REF_BUDGET_S / (t_first * runs)) // 256 * 256)
+    for _ in range(args.warmup - 1):
+        wl.step(rows)
+    times = [wl.step(rows) for _ in range(args.steps)]
+    t = sum(times) / len(times)
     value = step_ops(rows) / t / 1e12
-    sample = f"{rows} of {M_TOKENS} tokens per step through all four layers (oracle port, numpy + BLAS)"
+    cfg = workload_config(1, world)
+    if rows != M_TOKENS:
+        cfg["cpu_tokens_per_step"] = rows
+    sample = f"{rows} of {M_TOKENS} tokens per step through all four layers: {what}"
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3 * M_TOKENS / rows,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4",
-        "data": "synthetic (seeded; config-1 shapes and value distributions)",
-        "config": workload_config(1, {"cpu_rows_per_step": rows}),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port", "sample": sample},
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "dtype": "int4", "data": "synthetic (seeded; config-1 shapes and value distributions)",
+        "config": cfg,
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": kind,
+                         "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -273,7 +310,8 @@ def run_reference(args, rank):
 # --------------------------------------------------------------------------- GPU arm
 
 def build_layers(device, seed, cfg_id=1):
-    """Quantized layers and device-resident inputs of one step of config `cfg_id`."""
+    """Quantized layers (the same weights on every rank) and device-resident inputs of
+    one step of config `cfg_id`."""
     import _int4
     gen = torch.Generator().manual_seed(seed)
     layers = []
@@ -299,37 +337,20 @@ def build_layers(device, seed, cfg_id=1):
         del w
         if (m, k) not in xs:
             xs[(m, k)] = synth_activation(m, k, gen, device)
+        layer["key"] = (m, k)
     return layers, xs
+
+
+def run_layer(l, x):
+    import _int4
+    if l["r"]:
+        return _int4.convrot_w4a4_linear_lora(x, l["qw"], l["ws"], l["bias"], l["adapters"], GROUP)
+    return _int4.convrot_w4a4_linear(x, l["qw"], l["ws"], l["bias"], GROUP)
 
 
 def device_step(layers, xs):
     """One step through the public API on device-resident inputs."""
-    import _int4
-    outs = []
-    for l in layers:
-        x = xs[(l["m"], l["k"])]
-        if l["r"]:
-            outs.append(_int4.convrot_w4a4_linear_lora(x, l["qw"], l["ws"], l["bias"], l["adapters"], GROUP))
-        else:
-            outs.append(_int4.convrot_w4a4_linear(x, l["qw"], l["ws"], l["bias"], GROUP))
-    return outs
-
-
-def nsplit_step(layers, xs, rank, world):
-    """Config 4's 12288->3072 layer (with its LoRA side path unfused: the split
-    applies to the int4 product) column-split over the ranks: each rank owns N/P
-    weight rows, all ranks see the same M=18432 tokens, an NCCL all-gather
-    assembles [M, N]. Returns (step_fn, ops of the whole layer, layer list)."""
-    from _int4.nsplit import convrot_w4a4_linear_nsplit, shard_rows
-    down = next(l for l in layers if l["k"] == 12288)
-    q, w, b = shard_rows(down["qw"], down["ws"], down["bias"], rank, world)
-    ops = 2 * down["m"] * down["n"] * down["k"]
-    lay = [dict(down, n_out=down["n"])]
-
-    def step(inputs=None):
-        src = xs if inputs is None else inputs
-        return [convrot_w4a4_linear_nsplit(src[(down["m"], down["k"])], q, w, b, GROUP)]
-    return step, ops, lay
+    return [run_layer(l, xs[l["key"]]) for l in layers]
 
 
 def time_kernel_batch(fns, iters, flush, stream):
@@ -384,10 +405,346 @@ def time_kernel(fn, iters, flush, stream):
     return total / iters
 
 
-def run_ours(args, rank, world, local_rank):
+def max_over_ranks(value: float, world: int, device) -> float:
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def timed_steps(step_fn, steps, flush, stream, world, device):
+    """Device ms per step (max over ranks) of `steps` steps, L2 flushed before each,
+    barrier + synchronize on both sides."""
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    events = []
+    for _ in range(steps):
+        flush()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        step_fn()
+        b.record(stream)
+        events.append((a, b))
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ms = sum(a.elapsed_time(b) for a, b in events) / steps
+    return max_over_ranks(ms, world, device)
+
+
+def graphed(step_fn, flush):
+    """Capture one call of step_fn in a CUDA graph; returns a replaying callable (and the graph)."""
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        outs = step_fn()
+    torch.cuda.synchronize()
+
+    def replay():
+        graph.replay()
+        return outs
+    for _ in range(2):
+        flush()
+        replay()
+    torch.cuda.synchronize()
+    return replay, graph
+
+
+def roofline_probes(layers, xs, device, flush, stream):
+    """Per-kernel roofline figures of config 1 on this GPU (rank 0, N = 1)."""
     import _int4
     from _int4 import cuda_loader as ck
     from _int4 import weight_cache
+    extras = {}
+    peaks, peak_src = load_peaks()
+    up = next(l for l in layers if l["name"] == "mlp_up")
+    m, k, n = up["m"], up["k"], up["n"]
+    iters = 10
+    # time the kernels the public linear runs for this layer: with the
+    # unpacked-weight cache on (default) and M > 128 that is the int8 pair GEMM
+    # on sign-extended codes, else the int4 pair GEMM on packed codes
+    x = xs[up["key"]]
+    unpacked = _int4._use_unpacked(x, up["qw"], GROUP)
+    if unpacked:
+        quant = ck.convrot_quant_int4_unpacked
+        wq = weight_cache.unpacked(up["qw"])
+        xq, xsc = quant(x, GROUP)
+        gemm = lambda: ck.int8_convrot_gemm(xq, wq, xsc, up["ws"], up["bias32"], torch.bfloat16)
+        gemm_name, code_bytes = "int8 pair GEMM on unpacked int4 codes", 1
+    else:
+        quant = ck.convrot_quant_int4
+        xq, xsc = quant(x, GROUP)
+        gemm = lambda: ck.int4_convrot_gemm(xq, up["qw"], xsc, up["ws"], up["bias32"], torch.bfloat16)
+        gemm_name, code_bytes = "int4 pair GEMM on packed codes", 0.5
+    gemm_ms = time_kernel(gemm, iters, flush, stream)
+    # 8 distinct activations (8 x 28 MB, well beyond L2), launched back to back
+    xq_in = [synth_activation(m, k, torch.Generator().manual_seed(100 + i), device) for i in range(8)]
+    quant_ms = time_kernel_batch([lambda x=x: quant(x, GROUP) for x in xq_in], iters, flush, stream)
+    del xq_in
+    gemm_ops = 2 * m * n * k
+    int8_peak = 2.0 * peaks["bf16_tflops"]           # dense int8 rate = 2x bf16 on B200
+    achieved = gemm_ops / (gemm_ms * 1e-3) / 1e12
+    extras["roofline"] = {
+        "kernel": f"int4_gemm_pair_kernel, {gemm_name} (MLP up 3072->12288, M=4608)",
+        "bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
+        "frac": achieved / int8_peak,
+        "peak_source": f"2 x {peak_src} bf16 burst ({peaks['bf16_tflops']} TFLOP/s): B200 dense int8 rate",
+        "ms_per_launch": gemm_ms,
+        "traffic": None,
+        "algorithmic_bytes": int(code_bytes * (m * k + n * k)) + 4 * m + 4 * n + 4 * n + 2 * m * n,
+        "w4a4_bytes": (m * k + n * k) // 2 + 4 * m + 4 * n + 4 * n + 2 * m * n,
+    }
+    qbytes = 2 * m * k + m * k // 2 + 4 * m          # W4A4 activation bytes (packed codes)
+    extras["quant_kernel"] = {
+        "kernel": f"convrot_quant_bf16_kernel{' (unpacked codes)' if unpacked else ''} (K=3072, M=4608)",
+        "bound": "hbm",
+        "achieved": qbytes / (quant_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+        "frac": qbytes / (quant_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "ms_per_launch": quant_ms,
+        "bytes": "2MK read + MK/2 + 4M written (packed-code bytes, whatever form the codes take)",
+        "timing": "8 launches back to back over distinct 28 MB inputs in one CUDA graph, per launch",
+    }
+    # small-M (weight-bound) layers at M = 1 / 16 / 64 / 128
+    sm = {}
+    for mm, kk, nn in ((1, 3072, 18432), (16, 3072, 18432), (64, 3072, 18432), (128, 3072, 18432),
+                       (1, 12288, 3072), (64, 12288, 3072)):
+        wsm = (torch.randn(nn, kk, device=device) * 0.02).to(torch.float16)
+        qsm, wssm = _int4.quantize_convrot_w4a4_weight(wsm, GROUP)
+        del wsm
+        copies = max(2, math.ceil(400e6 / qsm.numel()))          # distinct weight copies beyond L2
+        qsms = [qsm] + [qsm.roll(i, 0).contiguous() for i in range(1, copies)]
+        xsm = synth_activation(mm, kk, torch.Generator().manual_seed(5), device)
+        ms = time_kernel_batch([lambda q=q: _int4.convrot_w4a4_linear(xsm, q, wssm, None, GROUP) for q in qsms],
+                               iters, flush, stream)
+        del qsms
+        wbytes = nn * kk // 2 + 4 * nn + mm * kk * 2 + 2 * mm * nn
+        sm[f"M={mm} {kk}->{nn}"] = {"ms_per_call": ms, "achieved_gbs": wbytes / (ms * 1e-3) / 1e9,
+                                    "frac": wbytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"]}
+    first = sm["M=1 3072->18432"]
+    extras["small_m"] = {
+        "kernel": "public linear at M <= 128 (quantizer + int4 GEMV / swapped-tile GEMM), headline M=1 3072->18432",
+        "bound": "hbm", "achieved": first["achieved_gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+        "frac": first["frac"], "ms_per_launch": first["ms_per_call"],
+        "bytes": "packed weights + scales + bf16 activations + bf16 output",
+        "timing": "calls back to back over distinct weight copies (>= 400 MB) in one CUDA graph, per call",
+        "cases": sm,
+    }
+    return extras
+
+
+# ---------------------------------------------------------------- config 2: a Flux DiT step
+
+FLUX_SKIP = ("img_in", "time_in", "guidance_in", "txt_in", "final_layer")   # int4_loader.py:25-27 (flux2 list)
+
+
+class FluxDiT:
+    """Synthetic Flux-architecture DiT, random init.
+
+    19 double-stream and 38 single-stream blocks, hidden 3072, 24 heads x 128,
+    MLP ratio 4, RoPE over (t, h, w) axes of 16/56/56 dims. Every Linear with
+    in_features >= 512 whose name matches no entry of the reference loader's
+    flux skip list is an ``Int4ConvRotLinear`` (random packed codes and scales);
+    the others are bf16. Attention is torch SDPA; norms, modulation, GELU and
+    RoPE are torch ops in bf16 (fp32 inside the norms and RoPE).
+    """
+
+    def __init__(self, device, seed=0, double=19, single=38, hidden=3072, heads=24):
+        from _int4.linear import Int4ConvRotLinear
+        self.device, self.hidden, self.heads = device, hidden, heads
+        self.gen = torch.Generator(device=device).manual_seed(seed)
+        self.int4_layers = 0
+        self.Q = Int4ConvRotLinear
+
+        def lin(name, k, n):
+            if k >= 512 and not any(s in name for s in FLUX_SKIP):
+                mod = Int4ConvRotLinear(k, n, True, device=device)
+                lo = torch.randint(-7, 8, (n, k // 2), generator=self.gen, device=device, dtype=torch.int16)
+                hi = torch.randint(-7, 8, (n, k // 2), generator=self.gen, device=device, dtype=torch.int16)
+                mod._q.copy_(((lo & 0xF) | ((hi & 0xF) << 4)).to(torch.uint8).view(torch.int8))
+                mod._qs.copy_(torch.rand(n, generator=self.gen, device=device) * 2e-3 + 4e-3)
+                mod.bias.copy_(torch.randn(n, generator=self.gen, device=device) * 0.01)
+                self.int4_layers += 1
+                return mod
+            w = (torch.randn(n, k, generator=self.gen, device=device) * (1.0 / math.sqrt(k))).to(torch.bfloat16)
+            b = torch.zeros(n, device=device, dtype=torch.bfloat16)
+            return lambda x: torch.nn.functional.linear(x, w, b)
+
+        h = hidden
+        self.img_in, self.txt_in = lin("img_in", 64, h), lin("txt_in", 4096, h)
+        self.time_in = (lin("time_in.in_layer", 256, h), lin("time_in.out_layer", h, h))
+        self.guidance_in = (lin("guidance_in.in_layer", 256, h), lin("guidance_in.out_layer", h, h))
+        self.vector_in = (lin("vector_in.in_layer", 768, h), lin("vector_in.out_layer", h, h))
+        self.double = []
+        for i in range(double):
+            blk = {}
+            for s in ("img", "txt"):
+                blk[s] = {"mod": lin(f"double_blocks.{i}.{s}_mod.lin", h, 6 * h),
+                          "qkv": lin(f"double_blocks.{i}.{s}_attn.qkv", h, 3 * h),
+                          "proj": lin(f"double_blocks.{i}.{s}_attn.proj", h, h),
+                          "mlp0": lin(f"double_blocks.{i}.{s}_mlp.0", h, 4 * h),
+                          "mlp2": lin(f"double_blocks.{i}.{s}_mlp.2", 4 * h, h),
+                          "qn": torch.ones(128, device=device), "kn": torch.ones(128, device=device)}
+            self.double.append(blk)
+        self.single = [{"mod": lin(f"single_blocks.{i}.modulation.lin", h, 3 * h),
+                        "linear1": lin(f"single_blocks.{i}.linear1", h, 3 * h + 4 * h),
+                        "linear2": lin(f"single_blocks.{i}.linear2", h + 4 * h, h),
+                        "qn": torch.ones(128, device=device), "kn": torch.ones(128, device=device)}
+                       for i in range(single)]
+        self.final_mod = lin("final_layer.adaLN_modulation.1", h, 2 * h)
+        self.final = lin("final_layer.linear", h, 64)
+
+    @staticmethod
+    def _mlp_embed(pair, x):
+        return pair[1](torch.nn.functional.silu(pair[0](x)))
+
+    @staticmethod
+    def _timestep_embedding(t, dim=256, max_period=10000.0):
+        half = dim // 2
+        freqs = torch.exp(-math.log(max_period) * torch.arange(half, dtype=torch.float32, device=t.device) / half)
+        args = (t.float() * 1000.0)[:, None] * freqs[None]
+        return torch.cat([torch.cos(args), torch.sin(args)], dim=-1).to(torch.bfloat16)
+
+    def _rope(self, ids):
+        """cos/sin [L, 64] of the (t, h, w) position axes, 16/56/56 dims, theta 10000."""
+        parts = []
+        for axis, d in enumerate((16, 56, 56)):
+            freqs = 1.0 / (10000.0 ** (torch.arange(0, d, 2, dtype=torch.float64, device=ids.device) / d))
+            parts.append(ids[:, axis:axis + 1].double() * freqs[None])
+        ang = torch.cat(parts, dim=-1).float()
+        return torch.cos(ang), torch.sin(ang)
+
+    @staticmethod
+    def _apply_rope(x, cos, sin):
+        xf = x.float().reshape(*x.shape[:-1], -1, 2)
+        x0, x1 = xf[..., 0], xf[..., 1]
+        out = torch.stack([x0 * cos - x1 * sin, x0 * sin + x1 * cos], dim=-1)
+        return out.reshape(x.shape).to(x.dtype)
+
+    @staticmethod
+    def _rms(x, scale):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * scale).to(x.dtype)
+
+    def _ln_mod(self, x, shift, scale):
+        return torch.nn.functional.layer_norm(x, (self.hidden,), eps=1e-6) * (1 + scale) + shift
+
+    def _heads(self, qkv, qn, kn):
+        L = qkv.shape[0]
+        q, k, v = qkv.view(L, 3, self.heads, 128).permute(1, 2, 0, 3)
+        return self._rms(q, qn), self._rms(k, kn), v
+
+    def _attend(self, q, k, v, cos, sin):
+        q, k = self._apply_rope(q, cos, sin), self._apply_rope(k, cos, sin)
+        o = torch.nn.functional.scaled_dot_product_attention(q[None], k[None], v[None])[0]
+        return o.permute(1, 0, 2).reshape(q.shape[1], self.hidden)
+
+    def forward(self, latent, txt, y, t, guidance):
+        h = self.hidden
+        c, hh, ww = latent.shape[1], latent.shape[2] // 2, latent.shape[3] // 2
+        img = latent[0].view(c, hh, 2, ww, 2).permute(1, 3, 0, 2, 4).reshape(hh * ww, c * 4)
+        img = self.img_in(img)
+        txt = self.txt_in(txt[0])
+        vec = (self._mlp_embed(self.time_in, self._timestep_embedding(t))
+               + self._mlp_embed(self.guidance_in, self._timestep_embedding(guidance))
+               + self._mlp_embed(self.vector_in, y))
+        svec = torch.nn.functional.silu(vec)
+        n_txt = txt.shape[0]
+        ids = torch.zeros(n_txt + hh * ww, 3, device=latent.device)
+        ids[n_txt:, 1] = torch.arange(hh, device=latent.device).repeat_interleave(ww).float()
+        ids[n_txt:, 2] = torch.arange(ww, device=latent.device).repeat(hh).float()
+        cos, sin = self._rope(ids)
+        for blk in self.double:
+            mods = {s: blk[s]["mod"](svec).chunk(6, dim=-1) for s in ("img", "txt")}
+            streams = {"img": img, "txt": txt}
+            qkv = {}
+            for s in ("txt", "img"):
+                sh, sc, _, _, _, _ = mods[s]
+                qkv[s] = self._heads(blk[s]["qkv"](self._ln_mod(streams[s], sh, sc)), blk[s]["qn"], blk[s]["kn"])
+            q, k, v = (torch.cat([qkv["txt"][i], qkv["img"][i]], dim=1) for i in range(3))
+            attn = self._attend(q, k, v, cos, sin)
+            outs = {"txt": attn[:n_txt], "img": attn[n_txt:]}
+            for s in ("txt", "img"):
+                _, _, g1, sh2, sc2, g2 = mods[s]
+                x = streams[s] + g1 * blk[s]["proj"](outs[s])
+                mlp = blk[s]["mlp2"](torch.nn.functional.gelu(blk[s]["mlp0"](self._ln_mod(x, sh2, sc2)),
+                                                              approximate="tanh"))
+                streams[s] = x + g2 * mlp
+            img, txt = streams["img"], streams["txt"]
+        x = torch.cat([txt, img], dim=0)
+        for blk in self.single:
+            sh, sc, g = blk["mod"](svec).chunk(3, dim=-1)
+            lin1 = blk["linear1"](self._ln_mod(x, sh, sc))
+            q, k, v = self._heads(lin1[:, :3 * h], blk["qn"], blk["kn"])
+            attn = self._attend(q, k, v, cos, sin)
+            mlp = torch.nn.functional.gelu(lin1[:, 3 * h:], approximate="tanh")
+            x = x + g * blk["linear2"](torch.cat([attn, mlp], dim=-1))
+        img = x[n_txt:]
+        sh, sc = self.final_mod(svec).chunk(2, dim=-1)
+        out = self.final(self._ln_mod(img, sh, sc))
+        return out.view(hh, ww, c, 2, 2).permute(2, 0, 3, 1, 4).reshape(1, c, hh * 2, ww * 2)
+
+
+def dit_step_leg(device, flush, stream, steps):
+    """Config 2: one denoising step (the DiT forward) at 1024^2, batch 1, CUDA graph."""
+    model = FluxDiT(device)
+    gen = torch.Generator(device=device).manual_seed(2)
+    latent = torch.randn(1, 16, 128, 128, generator=gen, device=device).to(torch.bfloat16)
+    txt = torch.randn(1, 512, 4096, generator=gen, device=device).to(torch.bfloat16)
+    y = torch.randn(1, 768, generator=gen, device=device).to(torch.bfloat16)
+    t = torch.full((1,), 0.5, device=device)
+    guidance = torch.full((1,), 3.5, device=device)
+    fwd = lambda: model.forward(latent, txt, y, t, guidance)
+    for _ in range(3):
+        out = fwd()
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all(), "DiT step produced non-finite values"
+    replay, graph = graphed(fwd, flush)
+    ms = timed_steps(replay, steps, flush, stream, 1, device)
+    del graph
+    return {"ms": ms, "int4_linears": model.int4_layers, "tokens": 4096 + 512,
+            "inputs": "latent [1,16,128,128], text [1,512,4096] ~ N(0,1), pooled [1,768] ~ N(0,1), t=0.5, "
+                      "guidance=3.5 (seeded)",
+            "launch": "CUDA graph replay, L2 flushed before each step"}
+
+
+# ---------------------------------------------------------------- config 4's layer, N-column split
+
+def nsplit_leg(device, rank, world, flush, stream, steps):
+    """Config 4's 12288->3072 layer (M = 18432, rank-64 LoRA) split by output columns:
+    each rank owns N/world weight rows, computes its columns for every token and the
+    all-gather assembles [M, N] on every rank. world = 1: the unsplit layer."""
+    import _int4
+    from _int4.nsplit import convrot_w4a4_linear_lora_nsplit, shard_adapters, shard_rows
+    layers, xs = build_layers(device, seed=4321, cfg_id=4)
+    down = next(l for l in layers if l["k"] == 12288)
+    x = xs[down["key"]]
+    ops = layer_ops(down["m"], down["k"], down["n"], down["r"])
+    one_gpu = None
+    if rank == 0:
+        fn1, g1 = graphed(lambda: run_layer(down, x), flush)
+        one_gpu = timed_steps(fn1, steps, flush, stream, 1, device)
+        del g1
+    if world == 1:
+        return {"value": ops / (one_gpu * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": one_gpu,
+                "layer": "M=18432 12288->3072 +LoRA r=64, unsplit"}
+    q, w, b = shard_rows(down["qw"], down["ws"], down["bias"], rank, world)
+    adapters = shard_adapters(down["adapters"], rank, world)
+    step = lambda: convrot_w4a4_linear_lora_nsplit(x, q, w, b, adapters, GROUP)
+    for _ in range(3):
+        out = step()
+    torch.cuda.synchronize()
+    ms = timed_steps(step, steps, flush, stream, world, device)
+    del out
+    return {"value": ops / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms, "one_gpu_ms": one_gpu,
+            "speedup_vs_one_gpu": one_gpu / ms if one_gpu else None,
+            "layer": f"M=18432 12288->3072 +LoRA r=64, N split x{world}, all-gather over NVLink"}
+
+
+# ---------------------------------------------------------------- the GPU arm
+
+def run_ours(args, rank, world, local_rank):
+    import _int4
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     assert _int4.is_available(), "libconvrot_b200.so must load on an sm_100 device"
@@ -398,166 +755,119 @@ def run_ours(args, rank, world, local_rank):
         flush_buf.fill_(1.0)
 
     cfg_id = args.config
-    layers, xs = build_layers(device, seed=1234 + rank, cfg_id=cfg_id)
-    ops_per_step = sum(layer_ops(l["m"], l["k"], l["n"], l["r"]) for l in layers)
-    if args.nsplit:
-        step_fn, ops_per_step, layers = nsplit_step(layers, xs, rank, world)
-    else:
-        step_fn = lambda inputs=None: device_step(layers, xs if inputs is None else inputs)
+    split = world > 1 and cfg_id != 2
+    layers, xs = _build_split(device, cfg_id, rank, world, split)
+    ops_total = sum(layer_ops(m, k, n, r) for _, m, k, n, r in WORKLOADS[cfg_id][1])
+    step_fn = lambda inputs=None: device_step(layers, xs if inputs is None else inputs)
     for _ in range(args.warmup):
         flush()
         step_fn()
     torch.cuda.synchronize()
-    if args.graph and not args.nsplit:
-        # Capture one step (the kernels of every layer) in a CUDA graph and
-        # replay it: per-launch host work (argument checks, tensor-map
-        # encoding) leaves the timed region, the device work is unchanged.
-        eager_fn = step_fn
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            graph_outs = eager_fn()
-        torch.cuda.synchronize()
-
-        def step_fn(inputs=None):
-            if inputs is not None:
-                return eager_fn(inputs)
-            graph.replay()
-            return graph_outs
-        for _ in range(2):
-            flush()
-            step_fn()
-        torch.cuda.synchronize()
+    graph = None
+    timed_fn = step_fn
+    if args.graph:
+        # One step (the kernels of every layer) as a CUDA graph: per-launch host
+        # work (argument checks, tensor-map encoding) leaves the timed region.
+        timed_fn, graph = graphed(step_fn, flush)
 
     # ---------------- timed region: K steps, barrier + sync on both sides
     sampler = ClockSampler(local_rank)
     sampler.start()
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
     t_region = time.time()
-    events = []
-    for _ in range(args.steps):
-        flush()
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        step_fn()
-        b.record(stream)
-        events.append((a, b))
-    torch.cuda.synchronize()
+    ms_per_step = timed_steps(timed_fn, args.steps, flush, stream, world, device)
     sampler.mark(t_region, time.time())
-    if world > 1:
-        torch.distributed.barrier()
     clocks = sampler.stop()
-    elapsed_ms = sum(a.elapsed_time(b) for a, b in events)
-    if world > 1:
-        t = torch.tensor([elapsed_ms], dtype=torch.float64, device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
-    ms_per_step = elapsed_ms / args.steps
-    # weak scaling: every rank ran a full step; N-split: the ranks shared one step
-    value = (1 if args.nsplit else world) * ops_per_step / (ms_per_step * 1e-3) / 1e12
+    value = ops_total / (ms_per_step * 1e-3) / 1e12
+    del graph
 
-    # ---------------- per-kernel roofline (dominant GEMM = MLP up), rank 0, config 1
     extras = {}
-    if rank == 0 and cfg_id == 1 and not args.nsplit:
-        peaks, peak_src = load_peaks()
-        up = next(l for l in layers if l["name"] == "mlp_up")
-        m, k, n = up["m"], up["k"], up["n"]
-        iters = 10
-        # time the kernels the public linear runs for this layer: with the
-        # unpacked-weight cache on (default) and M > 128 that is the int8 pair GEMM
-        # on sign-extended codes, else the int4 pair GEMM on packed codes
-        unpacked = _int4._use_unpacked(xs[(m, k)], up["qw"], GROUP)
-        if unpacked:
-            quant = ck.convrot_quant_int4_unpacked
-            wq = weight_cache.unpacked(up["qw"])
-            xq, xsc = quant(xs[(m, k)], GROUP)
-            gemm = lambda: ck.int8_convrot_gemm(xq, wq, xsc, up["ws"], up["bias32"], torch.bfloat16)
-            gemm_name, code_bytes = "int8 pair GEMM on unpacked int4 codes", 1
-            traffic_key = "int8_pair_unpacked_bytes_per_launch"
-        else:
-            quant = ck.convrot_quant_int4
-            xq, xsc = quant(xs[(m, k)], GROUP)
-            gemm = lambda: ck.int4_convrot_gemm(xq, up["qw"], xsc, up["ws"], up["bias32"], torch.bfloat16)
-            gemm_name, code_bytes = "int4_gemm_pair_kernel", 0.5
-            traffic_key = "int4_gemm_kernel_bytes_per_launch"
-        gemm_ms = time_kernel(gemm, iters, flush, stream)
-        # 8 distinct activations (8 x 28 MB, well beyond L2), launched back to back
-        xq_in = [synth_activation(m, k, torch.Generator().manual_seed(100 + i), device) for i in range(8)]
-        quant_ms = time_kernel_batch([lambda x=x: quant(x, GROUP) for x in xq_in], iters, flush, stream)
-        del xq_in
-        gemm_ops = 2 * m * n * k
-        int8_peak = 2.0 * peaks["bf16_tflops"]           # dense int8 rate = 2x bf16 on B200
-        achieved = gemm_ops / (gemm_ms * 1e-3) / 1e12
-        traffic = load_traffic()
-        extras["roofline"] = {
-            "kernel": f"int4_gemm_pair_kernel, {gemm_name} (MLP up 3072->12288, M=4608)",
-            "bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
-            "frac": achieved / int8_peak,
-            "peak_source": f"2 x {peak_src} bf16 burst ({peaks['bf16_tflops']} TFLOP/s): B200 dense int8 rate",
-            "ms_per_launch": gemm_ms,
-            "traffic": traffic.get(traffic_key) if traffic else None,
-            "algorithmic_bytes": int(code_bytes * (m * k + n * k)) + 4 * m + 4 * n + 4 * n + 2 * m * n,
-        }
-        qbytes = 2 * m * k + int(code_bytes * m * k) + 4 * m
-        extras["quant_kernel"] = {
-            "kernel": f"convrot_quant_bf16_kernel{' (unpacked codes)' if unpacked else ''} (K=3072, M=4608)",
-            "bound": "hbm",
-            "achieved": qbytes / (quant_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-            "frac": qbytes / (quant_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "ms_per_launch": quant_ms,
-            "timing": "8 launches back to back over distinct 28 MB inputs in one CUDA graph, per launch",
-            "traffic": traffic.get("convrot_quant_unpacked_bytes_per_launch" if unpacked else
-                                   "convrot_quant_bf16_kernel_bytes_per_launch") if traffic else None,
-        }
-        # small-M (weight-bound) layer: Flux modulation 3072 -> 18432 at M = 1
-        wsm = (torch.randn(18432, 3072, device=device) * 0.02).to(torch.float16)
-        qsm, wssm = _int4.quantize_convrot_w4a4_weight(wsm, GROUP)
-        del wsm
-        # 16 distinct weight copies (16 x 28 MB, beyond L2), launched back to back
-        qsms = [qsm] + [qsm.roll(i, 0).contiguous() for i in range(1, 16)]
-        x1 = synth_activation(1, 3072, torch.Generator().manual_seed(5), device)
-        x1q, x1s = ck.convrot_quant_int4(x1, GROUP)
-        sm_ms = time_kernel_batch([lambda q=q: ck.int4_convrot_gemm(x1q, q, x1s, wssm, None, torch.bfloat16)
-                                   for q in qsms], iters, flush, stream)
-        del qsms
-        sm_bytes = 3072 // 2 + 18432 * 3072 // 2 + 4 + 4 * 18432 + 2 * 18432
-        extras["small_m"] = {
-            "kernel": "int4_gemv_kernel (modulation 3072->18432, M=1)", "bound": "hbm",
-            "achieved": sm_bytes / (sm_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-            "frac": sm_bytes / (sm_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "ms_per_launch": sm_ms,
-            "timing": "16 launches back to back over distinct 28 MB weight copies in one CUDA graph, per launch",
-            "traffic": traffic.get("int4_gemv_kernel_bytes_per_launch") if traffic else None,
-        }
+    if world == 1 and cfg_id == 1 and args.extras:
+        extras.update(roofline_probes(layers, xs, device, flush, stream))
+    # ---------------- weak replicas: every rank runs all tokens
+    if world > 1 and cfg_id != 2 and args.extras:
+        full_layers, full_xs = build_layers(device, seed=1234, cfg_id=cfg_id)
+        fn, g = graphed(lambda: device_step(full_layers, full_xs), flush)
+        rms = timed_steps(fn, args.steps, flush, stream, world, device)
+        extras["replicas"] = {"value": world * ops_total / (rms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": rms,
+                              "scaling": "weak", "what": f"every rank runs all tokens of the step (x{world} work)"}
+        del g, full_layers, full_xs
+    # ---------------- config 4's 12288->3072 layer split by columns
+    if cfg_id == 1 and args.extras:
+        extras["nsplit"] = nsplit_leg(device, rank, world, flush, stream, min(args.steps, 50))
+    # ---------------- config 2: a full DiT denoising step (one GPU)
+    if world == 1 and cfg_id == 1 and args.extras:
+        dit = dit_step_leg(device, flush, stream, min(args.steps, 10))
+        lin_layers, lin_xs = build_layers(device, seed=7, cfg_id=2)
+        fn, g = graphed(lambda: device_step(lin_layers, lin_xs), flush)
+        lin_ms = timed_steps(fn, min(args.steps, 10), flush, stream, 1, device)
+        del g, lin_layers, lin_xs
+        dit.update({"linears_ms": lin_ms, "linears_share": lin_ms / dit["ms"],
+                    "linears_tops": sum(layer_ops(m, k, n, r) for _, m, k, n, r in WORKLOADS[2][1])
+                    / (lin_ms * 1e-3) / 1e12})
+        extras["dit_step_ms"] = dit["ms"]
+        extras["dit_step"] = dit
 
     # ---------------- end to end: host buffers in, host buffers out, through the public API
+    e2e = e2e_leg(layers, xs, device, stream, world, args.steps)
+    e2e_value = ops_total / (e2e["ms_per_step"] * 1e-3) / 1e12
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and cfg_id == 1 and args.cpu_seconds > 0:
+            cpu = cpu_sample(args.cpu_seconds)
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "strong" if split else "weak",
+            "vs_baseline": None, "dtype": "int4",
+            "data": "synthetic (seeded N(0,1) activations with 1% x20 outlier channels, N(0,0.02) weights)",
+            "config": workload_config(cfg_id, world if split else 1,
+                                      {"launch": "CUDA graph replay" if args.graph else "eager launches"}),
+            "gpu_launches": 2 * len(layers) * args.steps,
+            "clocks": clocks,
+            "e2e": {"value": e2e_value, "unit": UNIT, **e2e},
+            **extras,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+
+def _build_split(device, cfg_id, rank, world, split):
+    """Layers (replicated weights) and this rank's rows of every activation."""
+    if not split:
+        return build_layers(device, seed=1234, cfg_id=cfg_id)
+    layers, xs = build_layers(device, seed=1234, cfg_id=cfg_id)
+    shard = {}
+    for key, x in xs.items():
+        lo, hi = shard_range(x.shape[0], rank, world)
+        shard[key] = x[lo:hi].contiguous()
+    for l in layers:
+        l["m"] = shard[l["key"]].shape[0]
+    return layers, shard
+
+
+def e2e_leg(layers, xs, device, stream, world, steps):
+    """The step end to end through the public API: this rank's inputs from pinned host
+    buffers, outputs back to pinned host buffers, on three event-ordered streams."""
     host_in = {k: v.cpu().pin_memory() for k, v in xs.items()}
-    # one pinned buffer per output shape (config 2 has 304 outputs of 9 shapes); every
-    # layer's output still crosses PCIe each step
-    out_shapes = [(l["m"], l["n_out"] if "n_out" in l else l["n"]) for l in layers]
+    out_shapes = [(xs[l["key"]].shape[0], l["n"]) for l in layers]
+    # one pinned buffer per output shape; every layer's output still crosses PCIe each step
     host_buf = {sh: torch.empty(sh, dtype=torch.bfloat16).pin_memory() for sh in set(out_shapes)}
     host_out = [host_buf[sh] for sh in out_shapes]
     h2d = sum(v.numel() * v.element_size() for v in host_in.values())
     d2h = sum(v.numel() * v.element_size() for v in host_out)
-
-    # Uploads, the layers and the downloads run on three streams, ordered by events:
-    # a layer starts when its input has landed, its output leaves while the next
-    # layers compute, and host<->device copies use both PCIe directions at once.
     h2d_stream = torch.cuda.Stream(device)
     d2h_stream = torch.cuda.Stream(device)
     first_use = []
     for l in layers:
-        if (l["m"], l["k"]) not in first_use:
-            first_use.append((l["m"], l["k"]))
+        if l["key"] not in first_use:
+            first_use.append(l["key"])
 
-    def e2e_step_serial():
-        dev_in = {k: v.to(device, non_blocking=True) for k, v in host_in.items()}
-        outs = step_fn(dev_in)
-        for o, h in zip(outs, host_out):
-            h.copy_(o, non_blocking=True)
-
-    def e2e_step_pipelined():
-        import _int4
+    # Uploads, the layers and the downloads run on three streams, ordered by events:
+    # a layer starts when its input has landed, its output leaves while the next
+    # layers compute, and host<->device copies use both PCIe directions at once.
+    def e2e_step():
         dev_in, ready = {}, {}
         with torch.cuda.stream(h2d_stream):
             for key in first_use:
@@ -565,14 +875,10 @@ def run_ours(args, rank, world, local_rank):
                 ready[key] = torch.cuda.Event()
                 ready[key].record(h2d_stream)
         for l, h in zip(layers, host_out):
-            key = (l["m"], l["k"])
-            stream.wait_event(ready[key])
-            x = dev_in[key]
+            stream.wait_event(ready[l["key"]])
+            x = dev_in[l["key"]]
             x.record_stream(stream)
-            if l["r"]:
-                o = _int4.convrot_w4a4_linear_lora(x, l["qw"], l["ws"], l["bias"], l["adapters"], GROUP)
-            else:
-                o = _int4.convrot_w4a4_linear(x, l["qw"], l["ws"], l["bias"], GROUP)
+            o = run_layer(l, x)
             done = torch.cuda.Event()
             done.record(stream)
             d2h_stream.wait_event(done)
@@ -581,57 +887,24 @@ def run_ours(args, rank, world, local_rank):
                 h.copy_(o, non_blocking=True)
         stream.wait_stream(d2h_stream)          # the step ends when its results are on the host
 
-    e2e_step = e2e_step_serial if args.nsplit else e2e_step_pipelined
-
     for _ in range(2):
         e2e_step()
     torch.cuda.synchronize()
-    e2e_steps = max(3, min(args.steps, 10))
+    n = max(3, min(steps, 10))
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
     a.record(stream)
-    for _ in range(e2e_steps):
+    for _ in range(n):
         e2e_step()
     b.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = a.elapsed_time(b) / e2e_steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = (1 if args.nsplit else world) * ops_per_step / (e2e_ms * 1e-3) / 1e12
-
-    if rank == 0:
-        cpu_tops = None
-        if world == 1 and cfg_id == 1 and args.cpu_seconds > 0:
-            cpu_tops, _, _ = cpu_sample(args.cpu_rows, args.cpu_seconds)
-        par = (f"N-column split x{world} of the 12288->3072 layer, NCCL all-gather" if args.nsplit
-               else f"token-parallel replicas x{world}")
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": "strong" if args.nsplit else "weak",
-            "vs_baseline": None, "dtype": "int4",
-            "data": "synthetic (seeded N(0,1) activations with 1% x20 outlier channels, N(0,0.02) weights)",
-            "config": workload_config(cfg_id, {"parallelism": par,
-                                               "launch": "CUDA graph replay" if args.graph and not args.nsplit
-                                               else "eager launches"}),
-            "gpu_launches": 2 * len(layers) * args.steps,
-            "clocks": clocks,
-            "e2e": {"value": e2e_value, "unit": UNIT, "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "overlap": "serial" if args.nsplit else
-                               "uploads, layers and downloads on three streams (event-ordered)"},
-            **extras,
-        }
-        if cpu_tops is not None:
-            line["cpu_baseline"] = {"value": cpu_tops, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
-                                    "sample": f"{args.cpu_rows} tokens through all four layers, "
-                                              f"median over ~{args.cpu_seconds:.0f} s (oracle port)"}
-        print(json.dumps(line), flush=True)
+    ms = max_over_ranks(a.elapsed_time(b) / n, world, device)
+    return {"ms_per_step": ms, "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+            "bytes": "whole job (all ranks)",
+            "overlap": "uploads, layers and downloads on three streams (event-ordered)"}
 
 
 def run_case(args):
@@ -648,11 +921,14 @@ def run_case(args):
     qw, ws = _int4.quantize_convrot_w4a4_weight(w, GROUP)
     bias = torch.zeros(n, device=device)
     x = synth_activation(m, k, gen, device)
-    if args.case.endswith("_unpacked"):                # the captured kernel is the first launch
+    wpacked = qw
+    if args.case.endswith("_unpacked") or args.case.endswith("_a8"):   # the captured kernel is the first launch
         xq, xsc = ck.convrot_quant_int4_unpacked(x, GROUP)
-        qw = ck.int4_unpack(qw)
+        if args.case.endswith("_unpacked"):
+            qw = ck.int4_unpack(qw)
     else:
         xq, xsc = ck.convrot_quant_int4(x, GROUP)
+    flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
     for _ in range(args.iters):
         if args.case == "quant":
             ck.convrot_quant_int4(x, GROUP)
@@ -660,8 +936,11 @@ def run_case(args):
             ck.convrot_quant_int4_unpacked(x, GROUP)
         elif args.case == "mlp_up_unpacked":
             ck.int8_convrot_gemm(xq, qw, xsc, ws, bias, torch.bfloat16)
+        elif args.case == "mlp_up_a8":
+            ck.int4_convrot_gemm_a8(xq, wpacked, xsc, ws, bias, torch.bfloat16)
         else:
             ck.int4_convrot_gemm(xq, qw, xsc, ws, bias, torch.bfloat16)
+        flush_buf.fill_(1.0)          # evicts the output from L2: the launch's writes reach DRAM
     torch.cuda.synchronize()
     print(json.dumps({"case": args.case, "m": m, "k": k, "n": n, "iters": args.iters}))
 
@@ -672,15 +951,15 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-rows", type=int, default=256, help="tokens per CPU-baseline sample")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline time budget")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU-baseline time budget")
     ap.add_argument("--config", type=int, choices=sorted(WORKLOADS), default=1,
                     help="BASELINE config whose linear set is one step (default 1, the metric's config)")
-    ap.add_argument("--nsplit", action="store_true",
-                    help="config 4's 12288->3072 layer split by output columns over the ranks (strong scaling)")
+    ap.add_argument("--no-extras", dest="extras", action="store_false",
+                    help="only the main step (no probes, replicas, N-split or DiT legs)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="launch every kernel from the host each step instead of replaying a CUDA graph")
-    ap.add_argument("--case", choices=["mlp_up", "small_m", "quant", "mlp_up_unpacked", "quant_unpacked"], default=None,
+    ap.add_argument("--case", choices=["mlp_up", "small_m", "quant", "mlp_up_unpacked", "quant_unpacked", "mlp_up_a8"],
+                    default=None,
                     help="run one kernel --iters times (profiling helper) instead of the benchmark")
     ap.add_argument("--iters", type=int, default=3)
     args = ap.parse_args()
@@ -689,14 +968,12 @@ def main():
         return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    if args.nsplit:
-        args.config = 4
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        run_reference(args, rank)          # rank 0 only; no process group needed
+        run_reference(args, rank, world)          # rank 0 only; no process group needed
         return
     if world > 1:
         import datetime

@@ -38,6 +38,7 @@ _SIGNATURES = {
     "ck_int8_gemm_s32": [_P, _P, _P, _I, _I, _I, _P],
     "ck_int8_convrot_gemm_lora": [_P] * 5 + [_I, _P] + [_I] * 4 + [_P, _P, _I, ctypes.c_float, _P],
     "ck_int4_unpack": [_P, _P, ctypes.c_longlong, _I, _P],
+    "ck_int4_convrot_gemm_a8": [_P] * 5 + [_I, _P] + [_I] * 4 + [_P, _P, _I, ctypes.c_float, _P],
     "ck_convrot_quant_int4_unpacked": [_P, _I, _P, _P, _I, _I, _I, _P],
     "ck_convrot_w4a4_linear_unpacked_workspace_size": [_I, _I],
     "ck_convrot_w4a4_linear_unpacked": [_P, _I, _P, _P, _P, _I, _P] + [_I] * 5 + [_P, ctypes.c_size_t, _P],
@@ -192,6 +193,45 @@ def _gemm_lora(name, xq, wq, m, n, k, x_scale, w_scale, bias, out_dtype, lora_t,
                             bias_code, out.data_ptr(), m, n, k, _OUT_DTYPE_CODE[out_dtype], lora_t.data_ptr(),
                             lora_b.data_ptr(), r, float(lora_scale), _stream(xq))
     _check(name, rc)
+    return out
+
+
+def int4_convrot_gemm_a8(x_codes, w_packed, x_scale, w_scale, bias, out_dtype,
+                         lora_t=None, lora_b=None, lora_scale: float = 0.0):
+    """The int4 GEMM on int8 activation codes [M, K] (one sign-extended code per byte,
+    from convrot_quant_int4_unpacked) and packed int4 weights [N, K/2]: the same
+    accumulators and output bits as int4_convrot_gemm on the packed codes. With
+    lora_t / lora_b (bf16 [M, r] / [N, r]) the Dynamic-LoRA side path is fused as in
+    int4_convrot_gemm_lora. out_dtype torch.int32 returns the exact accumulators."""
+    lib = _load()
+    _require_cuda(x_codes, w_packed, x_scale, w_scale)
+    x_codes = x_codes.contiguous()
+    w_packed = w_packed.contiguous()
+    m, k = x_codes.shape
+    n, kp = w_packed.shape
+    if k != 2 * kp:
+        raise ValueError(f"K mismatch: codes {tuple(x_codes.shape)} packed weights {tuple(w_packed.shape)}")
+    codes = {**_OUT_DTYPE_CODE, torch.int32: 3}
+    if out_dtype not in codes:
+        raise ValueError(f"A8 gemm output dtype must be float32/bfloat16/int32, got {out_dtype}")
+    x_scale = x_scale.to(torch.float32).contiguous()
+    w_scale = w_scale.to(torch.float32).contiguous()
+    bias, bias_ptr, bias_code = _bias_arg(bias)
+    lt_ptr = lb_ptr = 0
+    r = 0
+    if lora_t is not None:
+        _require_cuda(lora_t, lora_b)
+        lora_t = lora_t.to(torch.bfloat16).contiguous()
+        lora_b = lora_b.to(torch.bfloat16).contiguous()
+        r = lora_t.shape[1]
+        if tuple(lora_t.shape) != (m, r) or tuple(lora_b.shape) != (n, r):
+            raise ValueError(f"LoRA shapes {tuple(lora_t.shape)} / {tuple(lora_b.shape)} do not match M={m}, N={n}")
+        lt_ptr, lb_ptr = lora_t.data_ptr(), lora_b.data_ptr()
+    out = torch.empty((m, n), dtype=out_dtype, device=x_codes.device)
+    rc = lib.ck_int4_convrot_gemm_a8(x_codes.data_ptr(), w_packed.data_ptr(), x_scale.data_ptr(),
+                                     w_scale.data_ptr(), bias_ptr, bias_code, out.data_ptr(), m, n, k,
+                                     codes[out_dtype], lt_ptr, lb_ptr, r, float(lora_scale), _stream(x_codes))
+    _check("ck_int4_convrot_gemm_a8", rc)
     return out
 
 

@@ -1137,10 +1137,10 @@ struct LoraArgs {
     float scale = 0.0f;
 };
 
-template <int BN, bool SWAP, int OUT, bool STAGED, bool LORA, bool I8 = false>
+template <int BN, bool SWAP, int OUT, bool STAGED, bool LORA, bool I8 = false, bool A8 = false>
 int launch_pair_impl(const void* Xp, const void* Wp, const float* xs, const float* ws, BiasRef bias,
                      void* out, int M, int N, int K, const LoraArgs& lora, cudaStream_t stream) {
-    using Cfg = PairCfg<BN, STAGED, SWAP, LORA, I8>;
+    using Cfg = PairCfg<BN, STAGED, SWAP, LORA, I8, A8>;
     const void* a_ptr = SWAP ? Wp : Xp;
     const void* b_ptr = SWAP ? Xp : Wp;
     const int rows_a = SWAP ? N : M;
@@ -1150,16 +1150,21 @@ int launch_pair_impl(const void* Xp, const void* Wp, const float* xs, const floa
     memset(&tlt, 0, sizeof(tlt));
     memset(&tlb, 0, sizeof(tlb));
     // (the packed-int4 map of 2K codes is the int8 map of K values: K bytes a row)
+    // (A8: int8 activation codes, K bytes a row; the expanders read the packed
+    // weights through plain loads, so they need no map)
     const int kcodes = I8 ? 2 * K : K;
-    if (!make_packed_tmap(&ta, a_ptr, rows_a, kcodes, 128) ||
-        !make_packed_tmap(&tb, b_ptr, rows_b, kcodes, BN / 2))
+    if (A8) memset(&tb, 0, sizeof(tb));
+    const bool maps_ok = A8 ? make_packed_tmap(&ta, a_ptr, rows_a, 2 * K, 128)
+                            : make_packed_tmap(&ta, a_ptr, rows_a, kcodes, 128) &&
+                                  make_packed_tmap(&tb, b_ptr, rows_b, kcodes, BN / 2);
+    if (!maps_ok)
         return fail("cuTensorMapEncodeTiled failed (pointer not 16-byte aligned or driver entry point missing)");
     if (STAGED && !make_out_tmap(&to, out, M, N))
         return fail("cuTensorMapEncodeTiled failed for the output");
     if (LORA && (!make_bf16_tmap(&tlt, lora.t, M, lora.rank, 128) ||
                  !make_bf16_tmap(&tlb, lora.b, N, lora.rank, BN / 2)))
         return fail("cuTensorMapEncodeTiled failed for the LoRA operands");
-    auto kernel = int4_gemm_pair_kernel<BN, SWAP, OUT, STAGED, LORA, I8>;
+    auto kernel = int4_gemm_pair_kernel<BN, SWAP, OUT, STAGED, LORA, I8, A8>;
     cudaError_t e = ensure_smem(kernel, Cfg::kSmemBytes);
     if (e != cudaSuccess) return static_cast<int>(e);
     const int tiles_a = (rows_a + 255) / 256;
@@ -1182,7 +1187,7 @@ int launch_pair_impl(const void* Xp, const void* Wp, const float* xs, const floa
     cfg.attrs = attr;
     cfg.numAttrs = 2;
     e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, tlt, tlb, xs, ws, bias, out, M, N, K, tiles_a,
-                           static_cast<int>(num_tiles), lora.scale);
+                           static_cast<int>(num_tiles), lora.scale, b_ptr);
     if (e != cudaSuccess) return static_cast<int>(e);
     return static_cast<int>(cudaGetLastError());
 }
@@ -1294,6 +1299,27 @@ int dispatch_gemm_i8(const void* X, const void* W, const float* xs, const float*
     return launch_pair_impl<256, false, OUT, false, false, true>(X, W, xs, ws, bias, out, M, N, K, LoraArgs(), stream);
 }
 
+// int4 layers on int8 activation codes and packed weights (the A8 form): 256 x 256
+// pair tiles, or 256 x 128 when 256-column tiles leave most CTA pairs idle; with
+// a LoRA side path the same rule (256-column LoRA tiles hold one accumulator pair).
+template <int OUT>
+int dispatch_gemm_a8(const void* X8, const void* Wp, const float* xs, const float* ws, BiasRef bias,
+                     void* out, int M, int N, int K, const LoraArgs& lora, cudaStream_t stream) {
+    const long tiles256 = static_cast<long>((M + 255) / 256) * ((N + 255) / 256);
+    if (lora.rank > 0) {
+        if (2 * tiles256 >= sm_count())
+            return launch_pair_impl<256, false, OUT, false, true, false, true>(X8, Wp, xs, ws, bias, out, M, N, K,
+                                                                               lora, stream);
+        return launch_pair_impl<128, false, OUT, false, true, false, true>(X8, Wp, xs, ws, bias, out, M, N, K,
+                                                                           lora, stream);
+    }
+    if (2 * tiles256 >= sm_count() / 2)
+        return launch_pair_impl<256, false, OUT, false, false, false, true>(X8, Wp, xs, ws, bias, out, M, N, K,
+                                                                            lora, stream);
+    return launch_pair_impl<128, false, OUT, false, false, false, true>(X8, Wp, xs, ws, bias, out, M, N, K,
+                                                                        lora, stream);
+}
+
 int check_gemm_args(const void* Xp, const void* Wp, int M, int N, int K) {
     if (M < 0 || N < 0 || K <= 0) return fail("M, N must be >= 0 and K > 0");
     if (K % 32 != 0) return fail("K must be a multiple of 32");
@@ -1395,18 +1421,47 @@ int check_linear_args(const void* x, int in_dtype, const void* Wp, const void* w
     return 0;
 }
 
-// Workspace of the fused linear: packed activation codes [M, K/2], then the
+// Workspace of the packed-code linear: activation codes [M, K/2], then the
 // row scales [M] f32, each from a 256-byte boundary.
-size_t linear_workspace_bytes(int M, int K) {
+size_t packed_linear_workspace_bytes(int M, int K) {
     const size_t codes = (static_cast<size_t>(M) * static_cast<size_t>(K / 2) + 255) & ~static_cast<size_t>(255);
+    return codes + ((static_cast<size_t>(M) * 4 + 255) & ~static_cast<size_t>(255));
+}
+
+// Rows from which the fused linear takes the A8 form (int8 activation codes,
+// packed weights): the tensor-core pipeline without activation expansion.
+constexpr int kA8MinRows = 129;
+
+bool a8_eligible(int in_dtype, int M, int K, int G) {
+    return in_dtype == 1 && (G == 64 || G == 256) && K % 256 == 0 && K / 256 <= kQ5MaxTiles && M >= kA8MinRows;
+}
+
+// Workspace of ck_convrot_w4a4_linear: one int8 per code when the call may take
+// the A8 form (M >= kA8MinRows; the size cannot depend on the dtype, which the
+// size query does not see), else packed codes.
+size_t linear_workspace_bytes(int M, int K) {
+    if (M < kA8MinRows) return packed_linear_workspace_bytes(M, K);
+    const size_t codes = (static_cast<size_t>(M) * static_cast<size_t>(K) + 255) & ~static_cast<size_t>(255);
     return codes + ((static_cast<size_t>(M) * 4 + 255) & ~static_cast<size_t>(255));
 }
 
 // Rotate + quantize x into the workspace, then the int4 GEMM (or GEMV) with the
 // bias read in its own dtype. The second launch is a programmatic dependent of
-// the first, so its prologue and weight prefetch overlap the quantizer.
+// the first, so its prologue and weight prefetch overlap the quantizer. With
+// allow_a8 and many bf16 rows the codes are written one per byte and the A8
+// GEMM expands only the packed weights (the same accumulators and output bits).
 int run_linear(const void* x, int in_dtype, const void* Wp, const float* ws, BiasRef bias, void* out,
-               int out_dtype, int M, int N, int K, int G, unsigned char* workspace, cudaStream_t stream) {
+               int out_dtype, int M, int N, int K, int G, unsigned char* workspace, cudaStream_t stream,
+               bool allow_a8) {
+    if (allow_a8 && a8_eligible(in_dtype, M, K, G)) {
+        unsigned char* q = workspace;
+        float* xs = reinterpret_cast<float*>(q + ((static_cast<size_t>(M) * K + 255) & ~static_cast<size_t>(255)));
+        int rc = G == 256 ? launch_quant_bf16_tiles<256, 4, true>(x, q, xs, M, K, stream)
+                          : launch_quant_bf16_tiles<64, 4, true>(x, q, xs, M, K, stream);
+        if (rc != 0) return rc;
+        if (out_dtype == 1) return dispatch_gemm_a8<kOutBF16>(q, Wp, xs, ws, bias, out, M, N, K, LoraArgs(), stream);
+        return dispatch_gemm_a8<kOutF32>(q, Wp, xs, ws, bias, out, M, N, K, LoraArgs(), stream);
+    }
     void* q = workspace;
     float* xs = reinterpret_cast<float*>(workspace + ((static_cast<size_t>(M) * (K / 2) + 255) & ~static_cast<size_t>(255)));
     int rc = G == 256 ? launch_quant_g<256>(x, in_dtype, q, xs, M, K, stream)
@@ -1477,7 +1532,7 @@ CONVROT_API int ck_convrot_w4a4_linear(const void* x, int in_dtype, const void* 
         return fail("workspace smaller than ck_convrot_w4a4_linear_workspace_size(M, K)");
     return run_linear(x, in_dtype, Wp, static_cast<const float*>(wscale), BiasRef{bias, bias_dtype}, out,
                       out_dtype, M, N, K, G, static_cast<unsigned char*>(workspace),
-                      static_cast<cudaStream_t>(stream));
+                      static_cast<cudaStream_t>(stream), true);
 }
 
 CONVROT_API int ck_int4_convrot_gemm_lora(const void* Xp, const void* Wp, const void* xscale, const void* wscale,
@@ -1605,6 +1660,39 @@ CONVROT_API int ck_int8_gemm_s32(const void* X, const void* W, void* acc, int M,
     if (!acc) return fail("null accumulator pointer");
     return dispatch_gemm_i8<kOutS32>(X, W, nullptr, nullptr, BiasRef{nullptr, 0}, acc, M, N, K,
                                      static_cast<cudaStream_t>(stream));
+}
+
+CONVROT_API int ck_int4_convrot_gemm_a8(const void* X8, const void* Wp, const void* xscale, const void* wscale,
+                                        const void* bias, int bias_dtype, void* out, int M, int N, int K,
+                                        int out_dtype, const void* lora_t, const void* lora_b, int rank,
+                                        float lora_scale, void* stream) {
+    if (M < 0 || N < 0 || K <= 0 || K % 128 != 0 || K > 65536)
+        return fail("M, N must be >= 0 and K a multiple of 128 in [128, 65536]");
+    if (out_dtype != 0 && out_dtype != 1 && out_dtype != 3) return fail("out_dtype must be 0 (f32), 1 (bf16) or 3 (s32)");
+    if (bias_dtype < 0 || bias_dtype > 2) return fail("bias_dtype must be 0 (f32), 1 (bf16) or 2 (f16)");
+    const bool with_lora = lora_t != nullptr || lora_b != nullptr;
+    if (with_lora && (rank < 8 || rank > 64 || rank % 8 != 0)) return fail("LoRA rank must be a multiple of 8 in [8, 64]");
+    if (with_lora && out_dtype == 3) return fail("the int32 accumulator output has no LoRA side path");
+    if (M == 0 || N == 0) return 0;
+    if (!X8 || !Wp || !out) return fail("null operand or output pointer");
+    if (out_dtype != 3 && (!xscale || !wscale)) return fail("null scale pointer");
+    if (!aligned16(X8) || !aligned16(Wp)) return fail("operands must be 16-byte aligned");
+    if (with_lora && (!lora_t || !lora_b || !aligned16(lora_t) || !aligned16(lora_b)))
+        return fail("LoRA operands must be non-null and 16-byte aligned");
+    LoraArgs lora;
+    if (with_lora) {
+        lora.t = lora_t;
+        lora.b = lora_b;
+        lora.rank = rank;
+        lora.scale = lora_scale;
+    }
+    const float* xs = static_cast<const float*>(xscale);
+    const float* ws = static_cast<const float*>(wscale);
+    const BiasRef b{bias, bias_dtype};
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (out_dtype == 1) return dispatch_gemm_a8<kOutBF16>(X8, Wp, xs, ws, b, out, M, N, K, lora, s);
+    if (out_dtype == 0) return dispatch_gemm_a8<kOutF32>(X8, Wp, xs, ws, b, out, M, N, K, lora, s);
+    return dispatch_gemm_a8<kOutS32>(X8, Wp, nullptr, nullptr, BiasRef{nullptr, 0}, out, M, N, K, lora, s);
 }
 
 CONVROT_API int ck_int4_unpack(const void* packed, void* codes, long long rows, int K, void* stream) {

@@ -31,6 +31,15 @@
 //   w8..w11   B expanders
 //   w12..w15  epilogue (TMEM lanes 32*(w%4) ..)
 //
+// A8 form (int8 activation codes, packed int4 weights): the activations come
+// from the quantizer as one sign-extended int8 per code and go by TMA
+// (cta_group::2) straight into shared memory, like the W8A8 tier; only the
+// weights stay packed in HBM. Expander warps load them (64 bytes of K per row
+// and stage) straight into registers, a stage ahead, and write each byte b as
+// the int8 pair (16*lo, 16*hi) in column order into a weight slot (128 B
+// swizzle); the accumulator is 16 * D. Shared-memory bandwidth bounds these
+// pipelines, so the packed bytes never pass through shared memory.
+//
 // Stage hand-off: expander warps arrive with CTA-scope release on a local
 // barrier (the MMA's own barrier in the even CTA, a forwarding barrier in the
 // odd one). A cluster-scope release costs a memory-barrier round trip, so the
@@ -39,6 +48,15 @@
 #pragma once
 
 namespace convrot {
+
+// A8 weight-slot ring depth and expander groups (stages taken in turn; the
+// depth must be a multiple of the groups).
+#ifndef CONVROT_A8_BSTAGES
+#define CONVROT_A8_BSTAGES 4
+#endif
+#ifndef CONVROT_A8_GROUPS
+#define CONVROT_A8_GROUPS 2
+#endif
 
 constexpr int kPairThreads = 16 * 32;
 constexpr uint32_t kTmemCols = 512;
@@ -50,9 +68,26 @@ constexpr uint32_t kEpiBarrier = 1;      // named barrier id of the epilogue war
 // I8: the W8A8 tier -- plain int8 operands, no nibble expansion: both operands
 // go by TMA (cta_group::2, completing on the even CTA's barrier) straight into
 // shared memory and the MMAs read them there.
-template <int BN, bool STAGED, bool SWAP, bool LORA = false, bool I8 = false>
+// A8: int4 layers with int8 activation codes (one per byte) and packed int4
+// weights expanded in shared memory (see the header).
+template <int BN, bool STAGED, bool SWAP, bool LORA = false, bool I8 = false, bool A8 = false>
 struct PairCfg {
     static constexpr int kBHalf = BN / 2;
+    static constexpr bool kASmem = I8 || A8;                       // A by TMA into shared memory (MMA SS)
+    // A8: packed weight ring (64 bytes of K a row per stage: 128 codes)
+    static constexpr int kPackedRowBytes = 64;                     // packed bytes of a weight row per stage
+    static constexpr int kPackedChunks = A8 ? kBHalf * kPackedRowBytes / 16 : 0;   // 16-byte chunks per stage
+    static constexpr int kA8ExpWarps = 8;                          // warps 4..11
+    // the expander warps form groups that take whole stages in turn, so several
+    // stages are expanded at once (each group's wait/expand/fence/arrive chain
+    // then only has to keep up with every kA8Groups-th stage)
+    static constexpr int kA8Groups = CONVROT_A8_GROUPS;
+    static constexpr int kA8GroupWarps = kA8ExpWarps / kA8Groups;
+    // A8 rings: activation tiles (the operand ring, kStages deep, A only) and
+    // expanded weight half-tiles (kBStages deep).
+    static constexpr int kBStages = A8 ? (LORA && BN > 128 ? 4 : CONVROT_A8_BSTAGES) : 0;
+    // A8: the odd CTA's expander warps arrive on the even CTA's barrier themselves
+    static constexpr bool kA8Direct = A8;
     // int8 form with 256 x 128 tiles (few tiles: small M or N): two 128-byte K
     // sub-tiles per stage, 8 MMAs per barrier wait and commit; a stage is
     // [A sub 0 | A sub 1 | B sub 0 | B sub 1]. (256-column tiles keep one: their
@@ -61,10 +96,11 @@ struct PairCfg {
     static constexpr int kStageK = kSubK * kPairBKP;               // operand bytes of K per stage
     static constexpr int kABytes = 128 * kPairBKP;                 // one sub-tile
     static constexpr int kBBytes = kBHalf * kPairBKP;
-    static constexpr int kStageBytes = I8 ? kSubK * (kABytes + kBBytes) : kABytes + 2 * kBBytes;
+    static constexpr int kStageBytes = I8 ? kSubK * (kABytes + kBBytes) : A8 ? kABytes : kABytes + 2 * kBBytes;
     static constexpr int kTmemStageCols = 2 * kPairBKP / 4;      // hi + lo bytes of a row, 4 per column
-    static constexpr int kMmasPerStage = (I8 ? kSubK : 2) * kPairBKP / 32;   // K = 32 bytes per MMA
-    static constexpr int kAccShift = I8 ? 0 : 8;                  // int4 halves accumulate 256 * D
+    static constexpr int kMmasPerStage = (I8 ? kSubK : A8 ? 1 : 2) * kPairBKP / 32;   // K = 32 bytes per MMA
+    // int4 halves accumulate 256 * D, A8's 16x-scaled weights 16 * D
+    static constexpr int kAccShift = I8 ? 0 : A8 ? 4 : 8;
     // bf16 output tile staged for the TMA store: 128 rows x BN cols, 64-col boxes
     static constexpr int kStagingBytes = STAGED ? 128 * BN * 2 : 0;
     // 227 KB per block, minus alignment slack, barriers and the staging tile
@@ -72,16 +108,17 @@ struct PairCfg {
     // this CTA's half of the LoRA up-projection rows
     static constexpr int kLoraTBytes = LORA ? 128 * 128 : 0;
     static constexpr int kLoraBBytes = LORA ? kBHalf * 128 : 0;
-    static constexpr int kSmemForStages = 227 * 1024 - 2048 - 4 * BN * 4 - kStagingBytes - kLoraTBytes - kLoraBBytes;
+    static constexpr int kSmemForStages = 227 * 1024 - 2048 - 4 * BN * 4 - kStagingBytes - kLoraTBytes - kLoraBBytes
+                                          - kBStages * kBBytes;
     // TMA ring (shared memory) and expanded-A ring (TMEM slots) are sized
     // independently: the loads may run further ahead than TMEM allows.
     static constexpr int kAccCols = LORA ? 2 * BN : BN;          // int32 accumulator (+ fp32 LoRA accumulator)
     // Accumulator buffers: with two, the next tile's MMAs run while the epilogue
     // drains the previous tile (the int8 tier has no A operand in TMEM, so both fit).
     // (256-column LoRA tiles need all 512 columns for one int32 + fp32 pair: one buffer)
-    static constexpr int kAccBufs = (I8 && !(LORA && BN > 128)) ? 2 : 1;
+    static constexpr int kAccBufs = (kASmem && !(LORA && BN > 128)) ? 2 : 1;
     static constexpr int kTmemStages0 =
-        I8 ? 16 : (static_cast<int>(kTmemCols) - kAccCols * kAccBufs) / kTmemStageCols;
+        kASmem ? 16 : (static_cast<int>(kTmemCols) - kAccCols * kAccBufs) / kTmemStageCols;
     static constexpr int kStagesBySmem = kSmemForStages / kStageBytes;
     static constexpr int kStagesCapped = kStagesBySmem < 16 ? kStagesBySmem : 16;
     // Swapped tiles: the three expander groups take TMA stages in turn, and TMA
@@ -92,10 +129,13 @@ struct PairCfg {
     // in order, so they need no such rounding.
     static constexpr int kStages = SWAP ? kStagesCapped - kStagesCapped % 3 : kStagesCapped;
     static constexpr int kTmemStages = kTmemStages0 < kStages ? kTmemStages0 : kStages;
-    static constexpr int kStagingOffset = kStages * kStageBytes;
+    static constexpr int kBexpOffset = kStages * kStageBytes;
+    static constexpr int kStagingOffset = kBexpOffset + kBStages * kBBytes;
     static constexpr int kLoraOffset = kStagingOffset + kStagingBytes;
     static constexpr int kBarOffset = kLoraOffset + kLoraTBytes + kLoraBBytes;
-    static constexpr int kNumBars = 4 * kStages + kTmemStages + 6;
+    // ready / forward barriers: one per weight slot in A8, per operand stage otherwise
+    static constexpr int kReadyStages = A8 ? kBStages : kStages;
+    static constexpr int kNumBars = 2 * kStages + 2 * kReadyStages + kTmemStages + 6 + kBStages;
     static constexpr int kMiscOffset = kBarOffset + kNumBars * 8;
     // per-tile column factors (scale, bias) x 2 tiles in flight
     static constexpr int kColOffset = kMiscOffset + 16;
@@ -105,12 +145,17 @@ struct PairCfg {
     // swapped (weight-bound) tiles: three groups of four warps take turns on
     // whole stages (A and B), otherwise four A and four B expander warps
     static constexpr int kExpGroups = SWAP ? 3 : 1;
-    static constexpr int kLocalArrivals = SWAP ? 4 : 8;            // expander warps per CTA and stage
-    static constexpr int kReadyCount = kLocalArrivals + 1;         // + the odd CTA's forwarder
+    static constexpr int kLocalArrivals = SWAP ? 4 : A8 ? kA8GroupWarps : 8;   // expander warps per CTA and stage
+    // + the odd CTA's forwarder (A8: each odd expander warp)
+    static constexpr int kReadyCount = kA8Direct ? 2 * kLocalArrivals : kLocalArrivals + 1;
     static_assert(BN >= 32 && BN <= 256 && BN % 32 == 0, "pair MMA N must be a multiple of 32 in [32, 256]");
     static_assert(kStages >= 2 && kTmemStages >= 2, "pipeline needs at least two stages");
     static_assert(!SWAP || (kExpGroups == 3 && kStages % 3 == 0), "swapped tiles: ring slots owned by one group");
     static_assert(!I8 || !SWAP, "the int8 form uses non-swapped tiles");
+    static_assert(!A8 || (!I8 && !SWAP && !STAGED), "A8: non-swapped tiles, direct stores");
+    static_assert(!A8 || kPackedChunks % (kA8GroupWarps * 32) == 0, "A8: whole chunks per expander thread");
+    static_assert(!A8 || kBStages % kA8Groups == 0,
+                  "A8: every weight / packed slot is always taken by the same expander group");
     static_assert(!LORA || kAccBufs * kAccCols <= static_cast<int>(kTmemCols), "accumulators fit TMEM");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
@@ -168,15 +213,15 @@ __device__ __forceinline__ void store_row32(void* out, size_t obase, int n, int 
 // LORA (not swapped): a rank <= 64 side path out += lora_scale * T[m, :] . B[n, :]
 // (T = x A^T precomputed, both bf16) on the tensor cores into a second, fp32
 // accumulator, added in the epilogue before the single output rounding.
-template <int BN, bool SWAP, int OUT, bool STAGED, bool LORA = false, bool I8 = false>
+template <int BN, bool SWAP, int OUT, bool STAGED, bool LORA = false, bool I8 = false, bool A8 = false>
 __global__ void __launch_bounds__(kPairThreads, 1)
 int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                       const __grid_constant__ CUtensorMap tmap_out,
                       const __grid_constant__ CUtensorMap tmap_lt, const __grid_constant__ CUtensorMap tmap_lb,
                       const float* __restrict__ xscale, const float* __restrict__ wscale,
                       BiasRef bias, void* __restrict__ out, int M, int N, int K,
-                      int tiles_a, int num_tiles, float lora_scale) {
-    using Cfg = PairCfg<BN, STAGED, SWAP, LORA, I8>;
+                      int tiles_a, int num_tiles, float lora_scale, const void* __restrict__ wraw) {
+    using Cfg = PairCfg<BN, STAGED, SWAP, LORA, I8, A8>;
     static_assert(!LORA || !SWAP, "the LoRA side path is fused into non-swapped tiles");
     static_assert(!STAGED || (OUT == kOutBF16 && !SWAP), "staged epilogue is for bf16, non-swapped tiles");
     extern __shared__ __align__(1024) unsigned char psmem_raw[];
@@ -184,14 +229,17 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         (reinterpret_cast<uintptr_t>(psmem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset);
     uint64_t* full_bar = bars;
-    uint64_t* ready_bar = bars + Cfg::kStages;
-    uint64_t* empty_bar = bars + 2 * Cfg::kStages;
-    uint64_t* fwd_bar = bars + 3 * Cfg::kStages;
-    uint64_t* tmem_free_bar = bars + 4 * Cfg::kStages;           // [kTmemStages]
+    uint64_t* empty_bar = bars + Cfg::kStages;
+    uint64_t* ready_bar = bars + 2 * Cfg::kStages;               // [kReadyStages]
+    uint64_t* fwd_bar = ready_bar + Cfg::kReadyStages;           // [kReadyStages]
+    uint64_t* tmem_free_bar = fwd_bar + Cfg::kReadyStages;       // [kTmemStages]
     uint64_t* acc_full_bar = tmem_free_bar + Cfg::kTmemStages;   // [2] per accumulator buffer
     uint64_t* acc_empty_bar = acc_full_bar + 2;                  // [2]
     uint64_t* lora_full_bar = acc_full_bar + 4;                  // even CTA: both CTAs' LoRA tiles landed
     uint64_t* lora_empty_bar = acc_full_bar + 5;                 // LoRA MMAs of the previous tile done
+    uint64_t* bempty_bar = acc_full_bar + 6;                     // A8: MMAs done with a weight slot [kBStages]
+    unsigned char* bexp_ring = smem + Cfg::kBexpOffset;
+    constexpr int kReadyStages = Cfg::kReadyStages;
     unsigned char* lora_t = smem + Cfg::kLoraOffset;
     unsigned char* lora_b = lora_t + Cfg::kLoraTBytes;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kMiscOffset);
@@ -203,7 +251,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
     const uint32_t cta = cluster_ctarank();
     const int cluster_id = blockIdx.x >> 1;
     const int num_clusters = gridDim.x >> 1;
-    const int row_bytes = I8 ? K : (K >> 1);                       // operand bytes per row
+    const int row_bytes = Cfg::kASmem ? K : (K >> 1);              // A operand bytes per row
     const int num_kt = (row_bytes + Cfg::kStageK - 1) / Cfg::kStageK;
     const int rows_a = SWAP ? N : M;
     // tiles of this cluster, and k-stage iterations over all of them
@@ -213,8 +261,10 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
     if (threadIdx.x == 0) {
         for (int s = 0; s < Cfg::kStages; ++s) {
             mbar_init(&full_bar[s], 1);
-            mbar_init(&ready_bar[s], Cfg::kReadyCount);
             mbar_init(&empty_bar[s], 1);
+        }
+        for (int s = 0; s < kReadyStages; ++s) {
+            mbar_init(&ready_bar[s], Cfg::kReadyCount);
             mbar_init(&fwd_bar[s], Cfg::kLocalArrivals);
         }
         for (int t = 0; t < Cfg::kTmemStages; ++t) mbar_init(&tmem_free_bar[t], 1);
@@ -224,9 +274,10 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         }
         mbar_init(lora_full_bar, 1);
         mbar_init(lora_empty_bar, 1);
+        for (int b = 0; b < Cfg::kBStages; ++b) mbar_init(&bempty_bar[b], 1);
         fence_mbar_init();
         tma_prefetch_desc(&tmap_a);
-        tma_prefetch_desc(&tmap_b);
+        if constexpr (!A8) tma_prefetch_desc(&tmap_b);           // (A8 reads its weights without a map)
         if constexpr (STAGED) tma_prefetch_desc(&tmap_out);
         if constexpr (LORA) { tma_prefetch_desc(&tmap_lt); tma_prefetch_desc(&tmap_lb); }
     }
@@ -243,22 +294,29 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         if constexpr (SWAP) {
             const int w_row0 = (t % tiles_a) * 256 + static_cast<int>(cta) * 128;
             for (int x = 0; x < num_kt * Cfg::kStageK; x += kPairBKP) tma_prefetch_l2_2d(&tmap_a, x, w_row0);
+        } else if constexpr (A8) {
+            // this CTA's weight rows are one contiguous block of packed bytes
+            const int w_row0 = (t / tiles_a) * BN + static_cast<int>(cta) * Cfg::kBHalf;
+            const int rows = N - w_row0 < Cfg::kBHalf ? N - w_row0 : Cfg::kBHalf;
+            if (rows > 0)
+                bulk_prefetch_l2(static_cast<const unsigned char*>(wraw) + static_cast<size_t>(w_row0) * (K >> 1),
+                                 static_cast<uint32_t>(rows) * static_cast<uint32_t>(K >> 1));
         } else {
             const int w_row0 = (t / tiles_a) * BN + static_cast<int>(cta) * Cfg::kBHalf;
             for (int x = 0; x < num_kt * Cfg::kStageK; x += kPairBKP) tma_prefetch_l2_2d(&tmap_b, x, w_row0);
         }
     };
-    if (!I8 && warp == 0 && lane == 0) prefetch_first_weights();
+    if (!Cfg::kASmem && warp == 0 && lane == 0) prefetch_first_weights();
     tc_fence_before();
     cluster_sync();                       // peer barriers initialised before any remote arrive
     tc_fence_after();
     // every operand, scale and output may belong to the previous kernel
     griddep_wait();
     griddep_launch_dependents();
-    // int8 form: warp 3 has no role, so it pulls the weight boxes of this CTA's
+    // int8 and A8 forms: warp 3 has no role, so it pulls the weight boxes of this CTA's
     // first tile into L2 ahead of the ring, after the sync (one prefetch per
     // k-stage; issued before the sync they held every warp back).
-    if (I8 && warp == 3 && lane == 0) prefetch_first_weights();
+    if (Cfg::kASmem && warp == 3 && lane == 0) prefetch_first_weights();
     const uint32_t tmem_base = *tmem_slot;
     const uint32_t tmem_a0 = tmem_base + Cfg::kAccCols * Cfg::kAccBufs;  // A stages follow the accumulators
     // fp32 LoRA accumulator (LORA only): the second half of each accumulator buffer
@@ -289,7 +347,14 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                         record_status(kStatusTimeoutProducer); ok = false; break;
                     }
                     unsigned char* st = smem + s * Cfg::kStageBytes;
-                    if constexpr (I8) {
+                    if constexpr (A8) {
+                        // int8 activation codes into the operand slot, both CTAs
+                        // completing on the even CTA's barrier (the packed weights have a
+                        // producer of their own, warp 2)
+                        const uint32_t full_leader = mapa_shared(smem_u32(&full_bar[s]), 0);
+                        if (cta == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * Cfg::kABytes);
+                        tma_load_2d_pair(st, &tmap_a, full_leader, kt * kPairBKP, a_row0);
+                    } else if constexpr (I8) {
                         // both CTAs' tiles complete on the even CTA's barrier
                         const uint32_t full_leader = mapa_shared(smem_u32(&full_bar[s]), 0);
                         if (cta == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * Cfg::kStageBytes);
@@ -308,7 +373,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                 }
             }
         }
-    } else if (warp == 1 && I8) {
+    } else if (warp == 1 && Cfg::kASmem) {
         if (cta == 0) {
             // ---------------- MMA issuer (even CTA), int8 form: the whole warp runs
             // the loop, so the stage index, barrier phase and operand descriptors
@@ -352,9 +417,19 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                         ok = false;
                         break;
                     }
+                    // A8: the weight half-tiles of both CTAs expanded into weight slot sb
+                    // (cluster scope: the odd CTA's half arrives from its forwarder)
+                    const int sb = A8 ? it % Cfg::kBStages : 0;
+                    if (A8 && !__all_sync(0xFFFFFFFFu,
+                                          mbar_wait_bounded<true>(&ready_bar[sb], (it / Cfg::kBStages) & 1))) {
+                        if (lane == 0) record_status(kStatusTimeoutMma);
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(smem + s * Cfg::kStageBytes);
-                    const uint32_t b_addr = a_addr + Cfg::kSubK * Cfg::kABytes;
+                    const uint32_t b_addr = A8 ? smem_u32(bexp_ring + sb * Cfg::kBBytes)
+                                               : a_addr + Cfg::kSubK * Cfg::kABytes;
                     // K-major, 128 B swizzle: the j-th 32-byte K step of a sub-tile is +2
                     // in the address field
                     uint64_t da[Cfg::kSubK], db[Cfg::kSubK];
@@ -369,6 +444,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                             mma_i8_ss_pair(acc_tmem, da[j >> 2] + 2 * (j & 3), db[j >> 2] + 2 * (j & 3),
                                            Cfg::kIdesc, (kt | j) != 0);
                         mma_commit_pair_multicast(&empty_bar[s], 0x3);
+                        if constexpr (A8) mma_commit_pair_multicast(&bempty_bar[sb], 0x3);
                     }
                     __syncwarp();
                 }
@@ -427,17 +503,81 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
             }
         }
     } else if (warp < 4) {
-        if (!I8 && cta == 1 && lane == 0) {
+        if (!I8 && !Cfg::kA8Direct && cta == 1 && lane == 0) {
             // ---------------- forwarders (odd CTA): local expansion done -> even CTA's MMA barrier
             const uint32_t ready_leader0 = mapa_shared(smem_u32(&ready_bar[0]), 0);
             for (int it = warp - 2; it < total_it; it += 2) {
-                const int s = it % Cfg::kStages;
-                const uint32_t ph = (it / Cfg::kStages) & 1;
+                const int s = it % kReadyStages;
+                const uint32_t ph = (it / kReadyStages) & 1;
                 if (!mbar_wait_bounded(&fwd_bar[s], ph)) { record_status(kStatusTimeoutExpand); break; }
                 mbar_arrive_cluster(ready_leader0 + s * 8);
             }
         }
-    } else if (!I8 && (warp < 12 || SWAP)) {
+    } else if (A8 && warp < 4 + Cfg::kA8ExpWarps) {
+        // ---------------- A8 weight expanders (warps 4..11): packed bytes from global
+        // memory into registers one group-stage ahead, then int8 pairs (16*lo, 16*hi)
+        // in column order, 128 B swizzled, into the weight slot
+        const uint32_t ready_leader0 = mapa_shared(smem_u32(ready_bar), 0);
+        const int group = (warp - 4) / Cfg::kA8GroupWarps;
+        const int et = ((warp - 4) % Cfg::kA8GroupWarps) * 32 + lane;
+        constexpr int kStride = Cfg::kA8GroupWarps * 32;
+        constexpr int kPer = A8 ? Cfg::kPackedChunks / kStride : 1;   // chunks per thread and stage
+        const unsigned char* wbytes = static_cast<const unsigned char*>(wraw);
+        const size_t wrow_bytes = static_cast<size_t>(K >> 1);
+        // chunk f of a stage: weight row f / 4, packed bytes 16 (f % 4) .. + 15 of its 64
+        auto load_stage = [&](int it, uint4 (&v)[kPer]) {
+            const int tp = cluster_id + (it / num_kt) * num_clusters;
+            const int w_row0 = (tp / tiles_a) * BN + static_cast<int>(cta) * Cfg::kBHalf;
+            const size_t col = static_cast<size_t>(it % num_kt) * Cfg::kPackedRowBytes;
+            #pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const int f = et + j * kStride;
+                const int n = w_row0 + (f >> 2);
+                v[j] = n < N ? __ldg(reinterpret_cast<const uint4*>(wbytes + static_cast<size_t>(n) * wrow_bytes +
+                                                                    col + (f & 3) * 16))
+                             : make_uint4(0u, 0u, 0u, 0u);
+            }
+        };
+        uint4 nxt[kPer];
+        if (group < total_it) load_stage(group, nxt);
+        for (int it = group; it < total_it; it += Cfg::kA8Groups) {
+            const int s = it % Cfg::kBStages;
+            uint4 cur[kPer];
+            #pragma unroll
+            for (int j = 0; j < kPer; ++j) cur[j] = nxt[j];
+            if (it + Cfg::kA8Groups < total_it) load_stage(it + Cfg::kA8Groups, nxt);
+            // the weight slot's previous MMAs are done with it
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded<true>(&bempty_bar[s], ((it / Cfg::kBStages) & 1) ^ 1))) {
+                record_status(kStatusTimeoutExpand); break;
+            }
+            unsigned char* dst = bexp_ring + s * Cfg::kBBytes;
+            #pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const int f = et + j * kStride;
+                const int row = f >> 2, c = f & 3, sw = row & 7;
+                const uint32_t w[4] = {cur[j].x, cur[j].y, cur[j].z, cur[j].w};
+                uint32_t o[8];
+                #pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const uint32_t lo = (w[e] << 4) & 0xF0F0F0F0u, hi = w[e] & 0xF0F0F0F0u;
+                    o[2 * e] = __byte_perm(lo, hi, 0x5140);          // codes 8e .. 8e+3
+                    o[2 * e + 1] = __byte_perm(lo, hi, 0x7362);      // codes 8e+4 .. 8e+7
+                }
+                unsigned char* drow = dst + row * kPairBKP;
+                *reinterpret_cast<uint4*>(drow + (((2 * c) ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                *reinterpret_cast<uint4*>(drow + (((2 * c + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                // the odd CTA's warps arrive on the even CTA's barrier: CTA-scope release
+                // after the proxy fence (a cluster-scope release costs thousands of cycles
+                // here and throttled the ring)
+                if (cta == 1) mbar_arrive_remote_cta(ready_leader0 + s * 8);
+                else mbar_arrive(&ready_bar[s]);
+            }
+        }
+    } else if (!I8 && !A8 && (warp < 12 || SWAP)) {
         // expansion done for stage s: local arrive (CTA-scope release)
         uint64_t* done_bar = (cta == 0) ? ready_bar : fwd_bar;
         const int quarter = warp & 3;

@@ -30,11 +30,18 @@ int fail(const char* msg);
 int check_linear_args(const void* x, int in_dtype, const void* Wp, const void* wscale, int bias_dtype,
                       const void* out, int out_dtype, int M, int N, int K, int G);
 
-// Bytes of scratch the fused linear uses for M rows of K.
+// Bytes of scratch the fused linear uses for M rows of K (one int8 per code
+// from the A8 form's row count on, packed codes below it).
 size_t linear_workspace_bytes(int M, int K);
 
-// Quantizer then GEMM/GEMV on `stream`, scratch at `workspace` (256-byte aligned).
+// Bytes of scratch of the packed-code form alone (allow_a8 = false below).
+size_t packed_linear_workspace_bytes(int M, int K);
+
+// Quantizer then GEMM/GEMV on `stream`, scratch at `workspace` (256-byte aligned,
+// linear_workspace_bytes or, without allow_a8, packed_linear_workspace_bytes).
+// allow_a8: many bf16 rows may take the A8 form (same output bits).
 int run_linear(const void* x, int in_dtype, const void* Wp, const float* ws, BiasRef bias, void* out,
-               int out_dtype, int M, int N, int K, int G, unsigned char* workspace, cudaStream_t stream);
+               int out_dtype, int M, int N, int K, int G, unsigned char* workspace, cudaStream_t stream,
+               bool allow_a8);
 
 }  // namespace convrot

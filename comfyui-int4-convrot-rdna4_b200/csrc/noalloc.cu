@@ -13,7 +13,9 @@
 // a library call that allocates.
 //
 // Rules for the caller:
-//   - sizes: linear_workspace_bytes(M, K) must not exceed kNoAllocScratchBytes
+//   - sizes: packed_linear_workspace_bytes(M, K) (the packed codes and row
+//     scales; this entry always quantizes to packed codes) must not exceed
+//     kNoAllocScratchBytes
 //     (checked before any CUDA call; -1 and a message otherwise);
 //   - nothing in the scratch needs initial contents: the quantizer writes every
 //     byte the GEMM reads, on every call, so the previous call's leftovers are
@@ -111,12 +113,12 @@ CONVROT_API int ck_convrot_w4a4_linear_noalloc(const void* x, int in_dtype, cons
                                                int M, int N, int K, int G, void* stream) {
     if (int rc = check_linear_args(x, in_dtype, Wp, wscale, bias_dtype, out, out_dtype, M, N, K, G)) return rc;
     if (M == 0 || N == 0) return 0;
-    if (linear_workspace_bytes(M, K) > kNoAllocScratchBytes)
+    if (packed_linear_workspace_bytes(M, K) > kNoAllocScratchBytes)
         return fail("M x K too large for the 128 MiB static scratch of ck_convrot_w4a4_linear_noalloc "
-                    "(needs ck_convrot_w4a4_linear_workspace_size(M, K) <= 134217728); "
+                    "(needs align256(M * K / 2) + align256(4 * M) <= 134217728); "
                     "use ck_convrot_w4a4_linear with a workspace, or split the rows");
     unsigned char* scratch = nullptr;
     if (int rc = noalloc_scratch(&scratch)) return rc;
     return run_linear(x, in_dtype, Wp, static_cast<const float*>(wscale), BiasRef{bias, bias_dtype}, out,
-                      out_dtype, M, N, K, G, scratch, static_cast<cudaStream_t>(stream));
+                      out_dtype, M, N, K, G, scratch, static_cast<cudaStream_t>(stream), false);
 }

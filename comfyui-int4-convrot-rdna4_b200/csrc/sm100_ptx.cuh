@@ -214,6 +214,15 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" :: "r"(cluster_addr) : "memory");
 }
 
+// Arrive on an mbarrier of another CTA of the cluster with CTA-scope release
+// (the PTX default semantics of a remote arrive). Used after a
+// fence.proxy.async.shared::cta for shared-memory operand tiles a pair MMA
+// reads: the cluster-scope release above costs a memory-barrier round trip of
+// thousands of cycles under load.
+__device__ __forceinline__ void mbar_arrive_remote_cta(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cluster.b64 _, [%0];" :: "r"(cluster_addr) : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05, CTA pairs
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"

@@ -55,8 +55,9 @@ int ck_int4_convrot_gemm(const void* Xp, const void* Wp, const void* xscale, con
                          void* stream);
 
 /* Workspace bytes that ck_convrot_w4a4_linear needs for M rows of K: the
- * packed activation codes [M, K/2] and the row scales [M] f32, each from a
- * 256-byte boundary. No reference counterpart (see below). */
+ * activation codes and the row scales [M] f32, each from a 256-byte boundary.
+ * The codes take [M, K/2] bytes (packed) below 129 rows and [M, K] bytes (one
+ * per code, for the A8 form below) from 129 rows on. No reference counterpart. */
 size_t ck_convrot_w4a4_linear_workspace_size(int M, int K);
 
 /* The whole W4A4 linear in one call: rotate + quantize x (as
@@ -67,7 +68,10 @@ size_t ck_convrot_w4a4_linear_workspace_size(int M, int K);
  * single HIP export does both. Differences from calling the two exports:
  *   - bias is read in its own dtype, bias_dtype 0 = f32, 1 = bf16, 2 = f16
  *     (widening is exact, so results equal an fp32-converted bias);
- *   - the GEMM launch is a programmatic dependent of the quantizer launch.
+ *   - the GEMM launch is a programmatic dependent of the quantizer launch;
+ *   - bf16 x with 129+ rows, K % 256 == 0 and G in {64, 256} takes the A8
+ *     form: codes written one per byte, then ck_int4_convrot_gemm_a8 (same
+ *     accumulators, same output bits).
  *   x [M, K] in_dtype (0 f32, 1 bf16, 2 f16); Wp [N, K/2]; wscale [N] f32;
  *   out [M, N] out_dtype (0 f32, 1 bf16); G in {16, 64, 256}, K % G == 0,
  *   K % 32 == 0; workspace 256-byte aligned, at least
@@ -166,6 +170,22 @@ int ck_int8_convrot_gemm(const void* X, const void* W, const void* xscale, const
 /* Raw exact int32 accumulators of the int8 product (no reference export; for
  * parity checks, like ck_int4_gemm_s32). */
 int ck_int8_gemm_s32(const void* X, const void* W, void* acc, int M, int N, int K, void* stream);
+
+/* The int4 GEMM on int8 activation codes (A8 form; no reference counterpart):
+ *   X8 [M, K] int8, one sign-extended code per byte (ck_convrot_quant_int4_unpacked),
+ *   Wp [N, K/2] packed int4 weights (the reference codec), both 16-byte aligned;
+ *   xscale [M], wscale [N] f32; bias [N] or NULL in bias_dtype (0 f32, 1 bf16, 2 f16);
+ *   out [M, N], out_dtype 0 = f32, 1 = bf16, 3 = int32 exact accumulators D
+ *   (scales and bias ignored); K % 128 == 0, K <= 65536.
+ * Optional Dynamic-LoRA side path as ck_int4_convrot_gemm_lora (lora_t, lora_b
+ * bf16 [M, rank] / [N, rank], rank a multiple of 8 in [8, 64]; both NULL: none).
+ * The weights stay packed in HBM and are expanded in shared memory; the
+ * activations go to the tensor cores as loaded. Same D, epilogue and output
+ * bits as the packed-code GEMM. */
+int ck_int4_convrot_gemm_a8(const void* X8, const void* Wp, const void* xscale, const void* wscale,
+                            const void* bias, int bias_dtype, void* out, int M, int N, int K,
+                            int out_dtype, const void* lora_t, const void* lora_b, int rank,
+                            float lora_scale, void* stream);
 
 /* Unpacked-code path (no reference counterpart). With both operands as one
  * sign-extended int8 per int4 code, sum_k x_k w_k is the int8 tensor-core product

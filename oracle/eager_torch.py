@@ -26,22 +26,22 @@ import torch
 _HADAMARD: dict = {}
 
 
-def hadamard(group: int, dtype: torch.dtype) -> torch.Tensor:
+def hadamard(group: int, dtype: torch.dtype, device="cpu") -> torch.Tensor:
     """kron(H4, ..., H4) / sqrt(group), H4 = ones - 2 * antidiag (``_int4/eager.py:20-46``)."""
-    key = (group, dtype)
+    key = (group, dtype, str(device))
     if key not in _HADAMARD:
         h4 = torch.ones(4, 4, dtype=torch.float64) - 2 * torch.eye(4, dtype=torch.float64).flip(1)
         h = h4
         while h.shape[0] < group:
             h = torch.kron(h, h4)
-        _HADAMARD[key] = (h / math.sqrt(group)).to(dtype)
+        _HADAMARD[key] = (h / math.sqrt(group)).to(device=device, dtype=dtype)
     return _HADAMARD[key]
 
 
 def rotate(x2d: torch.Tensor, group: int) -> torch.Tensor:
     """x [M, K] -> per-group x_g @ H in x.dtype (``_int4/eager.py:65-79``)."""
     m, k = x2d.shape
-    return torch.matmul(x2d.reshape(m, k // group, group), hadamard(group, x2d.dtype)).reshape(m, k)
+    return torch.matmul(x2d.reshape(m, k // group, group), hadamard(group, x2d.dtype, x2d.device)).reshape(m, k)
 
 
 def quantize_rowwise(x: torch.Tensor, qmax: int):

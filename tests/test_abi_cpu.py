@@ -87,9 +87,28 @@ def test_quant_rejects_bad_dtype_and_k(lib):
 def test_linear_workspace_size(lib):
     f = lib.ck_convrot_w4a4_linear_workspace_size
     up = lambda v: (v + 255) // 256 * 256
-    for m, k in [(1, 64), (4608, 3072), (7, 12288), (18432, 12288)]:
+    for m, k in [(1, 64), (7, 12288), (128, 3072)]:              # packed codes
         assert f(m, k) == up(m * k // 2) + up(4 * m)
+    for m, k in [(129, 3072), (4608, 3072), (18432, 12288)]:     # one int8 per code (A8 form)
+        assert f(m, k) == up(m * k) + up(4 * m)
     assert f(0, 3072) == 0
+
+
+def test_gemm_a8_rejects_bad_arguments(lib):
+    f = lib.ck_int4_convrot_gemm_a8
+    ok = dict(x=256, w=256, xs=256, ws=256, b=0, bd=0, out=256, m=4, n=8, k=256, od=1, lt=0, lb=0, r=0)
+
+    def call(**kw):
+        a = {**ok, **kw}
+        return f(a["x"], a["w"], a["xs"], a["ws"], a["b"], a["bd"], a["out"], a["m"], a["n"], a["k"], a["od"],
+                 a["lt"], a["lb"], a["r"], 1.0, None)
+    assert call(k=192) == -1 and b"128" in lib.ck_convrot_last_error()     # K % 128
+    assert call(od=2) == -1
+    assert call(bd=4) == -1
+    assert call(x=264) == -1 and b"aligned" in lib.ck_convrot_last_error()
+    assert call(lt=256, lb=256, r=12) == -1                                 # rank not a multiple of 8
+    assert call(lt=256, lb=256, r=64, od=3) == -1                           # no LoRA on raw accumulators
+    assert call(m=0) == 0 and call(n=0) == 0
 
 
 def test_linear_rejects_bad_arguments(lib):

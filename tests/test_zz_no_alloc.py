@@ -28,14 +28,20 @@ def lib():
     return cuda_loader.library()
 
 
+def packed_scratch_bytes(m, k):
+    """What the entry keeps in its scratch: packed codes and row scales, 256-byte aligned."""
+    up = lambda v: (v + 255) // 256 * 256
+    return up(m * k // 2) + up(4 * m)
+
+
 def test_noalloc_rejects_sizes_beyond_the_scratch(lib):
     """Checked on the host before any CUDA call (runs without a GPU)."""
     f = lib.ck_convrot_w4a4_linear_noalloc
     m, k = 32768, 8192                     # 128 MiB of codes + scales: over the limit
-    assert lib.ck_convrot_w4a4_linear_workspace_size(m, k) > SCRATCH
+    assert packed_scratch_bytes(m, k) > SCRATCH
     assert f(256, 1, 256, 256, 0, 0, 256, 1, m, 64, k, 256, None) == -1
     assert b"128 MiB" in lib.ck_convrot_last_error()
-    assert lib.ck_convrot_w4a4_linear_workspace_size(18432, 12288) <= SCRATCH
+    assert packed_scratch_bytes(18432, 12288) <= SCRATCH
     assert f(256, 1, 256, 256, 0, 0, 256, 1, 0, 64, k, 256, None) == 0      # empty: no launch
     assert f(256, 1, 256, 256, 0, 7, 256, 1, 4, 64, 256, 256, None) == -1   # bad bias dtype
 
@@ -75,7 +81,7 @@ def test_noalloc_near_the_scratch_limit(lib):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     m, k, n = 18432, 12288, 256
-    assert lib.ck_convrot_w4a4_linear_workspace_size(m, k) > (100 << 20)
+    assert packed_scratch_bytes(m, k) > (100 << 20)
     for seed in (11, 12):
         x, wq, ws, bias = _case(m, k, n, seed=seed)
         na = cuda_loader.convrot_w4a4_linear_noalloc(x, wq, ws, bias, torch.bfloat16, 256)
