@@ -436,7 +436,10 @@ def timed_steps(step_fn, steps, flush, stream, world, device):
 
 
 def graphed(step_fn, flush):
-    """Capture one call of step_fn in a CUDA graph; returns a replaying callable (and the graph)."""
+    """Capture one call of step_fn in a CUDA graph (after one eager call, which builds any
+    per-weight state outside the graph); returns a replaying callable and the graph."""
+    step_fn()
+    torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         outs = step_fn()
@@ -462,22 +465,27 @@ def roofline_probes(layers, xs, device, flush, stream):
     up = next(l for l in layers if l["name"] == "mlp_up")
     m, k, n = up["m"], up["k"], up["n"]
     iters = 10
-    # time the kernels the public linear runs for this layer: with the
-    # unpacked-weight cache on (default) and M > 128 that is the int8 pair GEMM
-    # on sign-extended codes, else the int4 pair GEMM on packed codes
+    # time the kernels the public linear runs for this layer: by default (packed
+    # weights, M > 128) the A8 form -- unpacked activation codes, packed weights
+    # expanded in the kernel; with the opt-in unpacked-weight cache the int8 pair
+    # GEMM on sign-extended codes of both operands; for few rows the packed GEMM
     x = xs[up["key"]]
-    unpacked = _int4._use_unpacked(x, up["qw"], GROUP)
-    if unpacked:
+    if _int4._use_unpacked(x, up["qw"], GROUP):
         quant = ck.convrot_quant_int4_unpacked
         wq = weight_cache.unpacked(up["qw"])
         xq, xsc = quant(x, GROUP)
         gemm = lambda: ck.int8_convrot_gemm(xq, wq, xsc, up["ws"], up["bias32"], torch.bfloat16)
-        gemm_name, code_bytes = "int8 pair GEMM on unpacked int4 codes", 1
+        gemm_name, code_bytes, form = "int8 pair GEMM on cached unpacked weight codes", (1, 1), "unpacked"
+    elif _int4._use_a8(x, GROUP):
+        quant = ck.convrot_quant_int4_unpacked
+        xq, xsc = quant(x, GROUP)
+        gemm = lambda: ck.int4_convrot_gemm_a8(xq, up["qw"], xsc, up["ws"], up["bias"], torch.bfloat16)
+        gemm_name, code_bytes, form = "A8 pair GEMM (int8 activation codes, packed int4 weights)", (1, 0.5), "a8"
     else:
         quant = ck.convrot_quant_int4
         xq, xsc = quant(x, GROUP)
         gemm = lambda: ck.int4_convrot_gemm(xq, up["qw"], xsc, up["ws"], up["bias32"], torch.bfloat16)
-        gemm_name, code_bytes = "int4 pair GEMM on packed codes", 0.5
+        gemm_name, code_bytes, form = "int4 pair GEMM on packed codes", (0.5, 0.5), "packed"
     gemm_ms = time_kernel(gemm, iters, flush, stream)
     # 8 distinct activations (8 x 28 MB, well beyond L2), launched back to back
     xq_in = [synth_activation(m, k, torch.Generator().manual_seed(100 + i), device) for i in range(8)]
@@ -493,12 +501,13 @@ def roofline_probes(layers, xs, device, flush, stream):
         "peak_source": f"2 x {peak_src} bf16 burst ({peaks['bf16_tflops']} TFLOP/s): B200 dense int8 rate",
         "ms_per_launch": gemm_ms,
         "traffic": None,
-        "algorithmic_bytes": int(code_bytes * (m * k + n * k)) + 4 * m + 4 * n + 4 * n + 2 * m * n,
-        "w4a4_bytes": (m * k + n * k) // 2 + 4 * m + 4 * n + 4 * n + 2 * m * n,
+        "algorithmic_bytes": (m * k + n * k) // 2 + 4 * m + 4 * n + 2 * n + 2 * m * n,
+        "bytes_read_as_launched": int(code_bytes[0] * m * k + code_bytes[1] * n * k) + 4 * m + 4 * n + 2 * n
+                                  + 2 * m * n,
     }
     qbytes = 2 * m * k + m * k // 2 + 4 * m          # W4A4 activation bytes (packed codes)
     extras["quant_kernel"] = {
-        "kernel": f"convrot_quant_bf16_kernel{' (unpacked codes)' if unpacked else ''} (K=3072, M=4608)",
+        "kernel": f"convrot_quant_bf16_kernel{' (unpacked codes)' if form != 'packed' else ''} (K=3072, M=4608)",
         "bound": "hbm",
         "achieved": qbytes / (quant_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
         "frac": qbytes / (quant_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "ms_per_launch": quant_ms,
@@ -780,9 +789,25 @@ def run_ours(args, rank, world, local_rank):
     value = ops_total / (ms_per_step * 1e-3) / 1e12
     del graph
 
+    # ---------------- end to end: host buffers in, host buffers out, through the public API
+    e2e = e2e_leg(layers, xs, device, stream, world, args.steps)
+    e2e_value = ops_total / (e2e["ms_per_step"] * 1e-3) / 1e12
+
     extras = {}
     if world == 1 and cfg_id == 1 and args.extras:
         extras.update(roofline_probes(layers, xs, device, flush, stream))
+        # the same step with the opt-in unpacked-weight cache (int8 form, 2x weight bytes)
+        from _int4 import weight_cache
+        weight_cache.enable(True)
+        try:
+            fn, g = graphed(lambda: device_step(layers, xs), flush)
+            cms = timed_steps(fn, args.steps, flush, stream, 1, device)
+            del g
+        finally:
+            weight_cache.enable(False)
+        extras["unpacked_cache"] = {"value": ops_total / (cms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": cms,
+                                    "what": "same step with the opt-in unpacked-weight cache (int8 pair GEMM on "
+                                            "sign-extended codes of both operands; twice the weight bytes)"}
     # ---------------- weak replicas: every rank runs all tokens
     if world > 1 and cfg_id != 2 and args.extras:
         full_layers, full_xs = build_layers(device, seed=1234, cfg_id=cfg_id)
@@ -807,9 +832,6 @@ def run_ours(args, rank, world, local_rank):
         extras["dit_step_ms"] = dit["ms"]
         extras["dit_step"] = dit
 
-    # ---------------- end to end: host buffers in, host buffers out, through the public API
-    e2e = e2e_leg(layers, xs, device, stream, world, args.steps)
-    e2e_value = ops_total / (e2e["ms_per_step"] * 1e-3) / 1e12
 
     if rank == 0:
         cpu = None

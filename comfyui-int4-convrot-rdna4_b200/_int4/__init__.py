@@ -44,27 +44,37 @@ __all__ = [
 
 # Output dtypes the GEMM epilogue writes directly; others compute f32 then cast.
 _NATIVE_OUT = frozenset({torch.float32, torch.bfloat16})
-# Rows from which a layer runs on unpacked codes (int8 pipeline); fewer tokens
-# keep the packed paths, which read each weight once as int4 -- except layers
-# with few output rows (N <= _FEW_ROWS_N: a dozen swapped 256-row tiles leave
-# most SMs idle), which run unpacked once M * K >= _FEW_ROWS_MIN_MK (measured on
-# 3072 x 3072 .. 12288 x 4096 weights; below it, and under 5 tokens where the
-# few-token GEMV streams the packed weights, the packed paths are as fast).
+# With the unpacked-weight cache switched on (opt-in), layers run on unpacked
+# codes (int8 pipeline) from this many rows, and few-row layers (N <= _FEW_ROWS_N:
+# a dozen swapped 256-row tiles leave most SMs idle) already from 5 tokens once
+# M * K >= _FEW_ROWS_MIN_MK (measured on 3072 x 3072 .. 12288 x 4096 weights).
+# Without it, ck_convrot_w4a4_linear picks the form itself: the A8 form (int8
+# activation codes, packed weights) for 129+ bf16 rows, packed codes below.
 _UNPACKED_MIN_ROWS = 129
 _FEW_ROWS_N = 4096
 _FEW_ROWS_MIN_MK = 8 * 12288
+# rows from which the LoRA linear runs the A8 form (the fused linear's threshold)
+_A8_MIN_ROWS = 129
 
 
 def _use_unpacked(x2d: torch.Tensor, qweight: torch.Tensor, convrot_groupsize: int) -> bool:
+    """Whether this call runs on cached unpacked weight codes (the opt-in cache)."""
+    if not weight_cache.enabled():
+        return False
     m, k = x2d.shape
     few_rows = qweight.shape[0] <= _FEW_ROWS_N and m >= 5 and m * k >= _FEW_ROWS_MIN_MK
     if m < _UNPACKED_MIN_ROWS and not few_rows:
         return False
-    return weight_cache.enabled() and cuda_loader.unpacked_path_supported(x2d, convrot_groupsize)
+    return cuda_loader.unpacked_path_supported(x2d, convrot_groupsize)
+
+
+def _use_a8(x2d: torch.Tensor, convrot_groupsize: int) -> bool:
+    return x2d.shape[0] >= _A8_MIN_ROWS and cuda_loader.unpacked_path_supported(x2d, convrot_groupsize)
 
 
 def set_unpacked_weights(enabled: bool = True) -> None:
-    """Allow (default) or forbid the cached unpacked weight copies (2x weight bytes)."""
+    """Opt in to (or out of, the default) cached unpacked weight copies: faster
+    many-token layers at twice the weight bytes."""
     weight_cache.enable(enabled)
 
 
@@ -123,11 +133,12 @@ def convrot_w4a4_linear(
     x2d = x.reshape(-1, shape[-1]).contiguous()
     out_dtype = x.dtype if x.dtype in _NATIVE_OUT else torch.float32
     if _use_unpacked(x2d, qweight, convrot_groupsize):
-        # many tokens: both operands as int8 codes on the int8 tensor-core pipeline
+        # opt-in cache: both operands as int8 codes on the int8 tensor-core pipeline
         # (same accumulators, same results); the weight's codes are cached
         codes = weight_cache.unpacked(qweight)
         out = cuda_loader.convrot_w4a4_linear_unpacked(x2d, codes, wscales, bias, out_dtype, convrot_groupsize)
     else:
+        # packed weights; the fused entry picks the A8 form for many bf16 rows
         out = cuda_loader.convrot_w4a4_linear(x2d, qweight, wscales, bias, out_dtype, convrot_groupsize)
     if out.dtype != x.dtype:
         out = out.to(x.dtype)
@@ -169,6 +180,9 @@ def convrot_w4a4_linear_lora(
         qact, x_scale = cuda_loader.convrot_quant_int4_unpacked(x2d, convrot_groupsize)
         out = cuda_loader.int8_convrot_gemm_lora(qact, weight_cache.unpacked(qweight), x_scale, wscales, bias,
                                                  out_dtype, lora_t, up, scale)
+    elif _use_a8(x2d, convrot_groupsize):
+        qact, x_scale = cuda_loader.convrot_quant_int4_unpacked(x2d, convrot_groupsize)
+        out = cuda_loader.int4_convrot_gemm_a8(qact, qweight, x_scale, wscales, bias, out_dtype, lora_t, up, scale)
     else:
         qact, x_scale = convrot_quant_int4(x2d, convrot_groupsize)
         out = int4_convrot_gemm_lora(qact, qweight, x_scale, wscales, bias, out_dtype, lora_t, up, scale)

@@ -1,14 +1,15 @@
 """Unpacked-code copies of packed int4 weights, one per live weight tensor.
 
-The int4 layer runs fastest on the int8 tensor-core pipeline with both operands
-as one sign-extended int8 per code (identical results: the accumulators are the
-same exact integers). Activations are quantized straight into that form; a
-weight is unpacked once, on first use, and the copy lives exactly as long as the
-packed tensor object it came from (a weak reference drops it). An in-place write
-to the packed tensor (its version counter moves) or a new storage refreshes the
-copy. The copy doubles the bytes of every weight that runs with more than a
-handful of tokens; ``enable(False)`` (or ``CONVROT_UNPACKED_WEIGHTS=0``) keeps
-only the packed weights and the in-kernel nibble expansion.
+Opt-in speed over memory: with both operands as one sign-extended int8 per
+code the int4 layer runs on the plain int8 tensor-core pipeline (identical
+results: the accumulators are the same exact integers), about a fifth faster
+than the default A8 form on many-token layers, at the price of a second,
+unpacked copy of every weight (twice the packed bytes). Off by default: the
+weights then stay packed int4 in HBM. ``enable(True)`` (or
+``CONVROT_UNPACKED_WEIGHTS=1``) turns it on. A weight is unpacked once, on
+first use, and the copy lives exactly as long as the packed tensor object it
+came from (a weak reference drops it); an in-place write to the packed tensor
+(its version counter moves) or a new storage refreshes the copy.
 """
 from __future__ import annotations
 
@@ -18,7 +19,7 @@ import weakref
 
 import torch
 
-_enabled = os.environ.get("CONVROT_UNPACKED_WEIGHTS", "1") != "0"
+_enabled = os.environ.get("CONVROT_UNPACKED_WEIGHTS", "0") == "1"
 _lock = threading.Lock()
 _cache: dict[int, tuple] = {}        # id(packed) -> (weakref, version, data_ptr, shape, codes)
 

@@ -55,7 +55,7 @@ namespace convrot {
 #define CONVROT_A8_BSTAGES 4
 #endif
 #ifndef CONVROT_A8_GROUPS
-#define CONVROT_A8_GROUPS 2
+#define CONVROT_A8_GROUPS 4
 #endif
 
 constexpr int kPairThreads = 16 * 32;
@@ -86,6 +86,7 @@ struct PairCfg {
     // A8 rings: activation tiles (the operand ring, kStages deep, A only) and
     // expanded weight half-tiles (kBStages deep).
     static constexpr int kBStages = A8 ? (LORA && BN > 128 ? 4 : CONVROT_A8_BSTAGES) : 0;
+    static constexpr int kBRing = A8 ? kBStages : 1;               // kBStages as a divisor (A8 code only)
     // A8: the odd CTA's expander warps arrive on the even CTA's barrier themselves
     static constexpr bool kA8Direct = A8;
     // int8 form with 256 x 128 tiles (few tiles: small M or N): two 128-byte K
@@ -419,9 +420,9 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                     }
                     // A8: the weight half-tiles of both CTAs expanded into weight slot sb
                     // (cluster scope: the odd CTA's half arrives from its forwarder)
-                    const int sb = A8 ? it % Cfg::kBStages : 0;
+                    const int sb = A8 ? it % Cfg::kBRing : 0;
                     if (A8 && !__all_sync(0xFFFFFFFFu,
-                                          mbar_wait_bounded<true>(&ready_bar[sb], (it / Cfg::kBStages) & 1))) {
+                                          mbar_wait_bounded<true>(&ready_bar[sb], (it / Cfg::kBRing) & 1))) {
                         if (lane == 0) record_status(kStatusTimeoutMma);
                         ok = false;
                         break;
@@ -541,13 +542,13 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         uint4 nxt[kPer];
         if (group < total_it) load_stage(group, nxt);
         for (int it = group; it < total_it; it += Cfg::kA8Groups) {
-            const int s = it % Cfg::kBStages;
+            const int s = it % Cfg::kBRing;
             uint4 cur[kPer];
             #pragma unroll
             for (int j = 0; j < kPer; ++j) cur[j] = nxt[j];
             if (it + Cfg::kA8Groups < total_it) load_stage(it + Cfg::kA8Groups, nxt);
             // the weight slot's previous MMAs are done with it
-            if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded<true>(&bempty_bar[s], ((it / Cfg::kBStages) & 1) ^ 1))) {
+            if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded<true>(&bempty_bar[s], ((it / Cfg::kBRing) & 1) ^ 1))) {
                 record_status(kStatusTimeoutExpand); break;
             }
             unsigned char* dst = bexp_ring + s * Cfg::kBBytes;

@@ -89,7 +89,7 @@ def test_linear_workspace_size(lib):
     up = lambda v: (v + 255) // 256 * 256
     for m, k in [(1, 64), (7, 12288), (128, 3072)]:              # packed codes
         assert f(m, k) == up(m * k // 2) + up(4 * m)
-    for m, k in [(129, 3072), (4608, 3072), (18432, 12288)]:     # one int8 per code (A8 form)
+    for m, k in [(129, 3072), (4608, 3072), (18432, 12288)]:    # one int8 per code (A8 form)
         assert f(m, k) == up(m * k) + up(4 * m)
     assert f(0, 3072) == 0
 

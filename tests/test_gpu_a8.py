@@ -120,3 +120,4 @@ def test_fused_linear_a8_vs_oracle(ck, m, k, n, g):
     ref = orc.convrot_w4a4_linear(bits(x)[rows], wp.cpu().numpy(), ws.cpu().numpy(), bias.float().cpu().numpy(), g)
     assert np.array_equal(bits(out)[rows], ref)
     assert ck.device_status() == 0
+

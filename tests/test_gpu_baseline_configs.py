@@ -3,8 +3,9 @@
 ``_int4.convrot_w4a4_linear`` is run on the full activation of each layer the
 benchmark times (config 0, the four config-1 layers at M = 4608, config 3's
 3840 <-> 15360 MLP at M = 1024 and 4096, config 4's LoRA layers at M = 18432),
-in both dispatch modes: the default (int8-form GEMM on unpacked codes for
-M > 128) and with the unpacked weights switched off (the packed int4 GEMM).
+in both dispatch modes: the default (packed weights: the A8 form, int8
+activation codes with in-kernel weight expansion, for M > 128) and with the
+opt-in unpacked-weight cache (the int8-form GEMM on unpacked codes).
 The quantizer is row-wise and every output row depends only on its own input
 row, so the oracle run on a seeded sample of 64 rows (first and last included)
 checks those rows exactly: bf16 bits equal. The LoRA layers are checked within
@@ -65,7 +66,7 @@ def sample_rows(m, seed):
     return np.unique(np.concatenate([rows, [0, m - 1]]))
 
 
-@pytest.mark.parametrize("unpacked", [True, False], ids=["default", "packed"])
+@pytest.mark.parametrize("unpacked", [False, True], ids=["default", "cached"])
 @pytest.mark.parametrize("name,m,k,n", SHAPES, ids=[s[0] for s in SHAPES])
 def test_public_linear_vs_oracle_on_sampled_rows(api, name, m, k, n, unpacked):
     x, w, bias = synth_layer(m, k, n, seed=m + k + n)
@@ -76,7 +77,7 @@ def test_public_linear_vs_oracle_on_sampled_rows(api, name, m, k, n, unpacked):
         out = api.convrot_w4a4_linear(x, qw, ws, bias=bias, convrot_groupsize=256)
         torch.cuda.synchronize()
     finally:
-        api.set_unpacked_weights(True)
+        api.set_unpacked_weights(False)
     rows = sample_rows(m, seed=n)
     ref = orc.convrot_w4a4_linear(bits(x)[rows], qw.cpu().numpy(), ws.cpu().numpy(),
                                   bias.float().cpu().numpy(), 256)
@@ -109,7 +110,7 @@ def check_lora_rows(got_bits, x_rows, qw, ws, bias, down, up, scale, t_unit):
     assert not bad.any(), f"{np.count_nonzero(bad)} sampled values outside the LoRA tolerance"
 
 
-@pytest.mark.parametrize("unpacked", [True, False], ids=["default", "packed"])
+@pytest.mark.parametrize("unpacked", [False, True], ids=["default", "cached"])
 @pytest.mark.parametrize("k,n", [(3072, 12288), (12288, 3072)], ids=["mlp_up", "mlp_down"])
 def test_public_lora_linear_config4_vs_oracle_on_sampled_rows(api, k, n, unpacked):
     """Config 4: M = 18432, rank-64 adapter, A, B ~ N(0, 0.01), alpha = 64."""
@@ -125,7 +126,7 @@ def test_public_lora_linear_config4_vs_oracle_on_sampled_rows(api, k, n, unpacke
         out = api.convrot_w4a4_linear_lora(x, qw, ws, bias, [(down, up, scale)], 256)
         torch.cuda.synchronize()
     finally:
-        api.set_unpacked_weights(True)
+        api.set_unpacked_weights(False)
     rows = sample_rows(m, seed=n + 1)
     check_lora_rows(bits(out)[rows], bits(x)[rows], qw.cpu().numpy(), ws.cpu().numpy(),
                     bias.float().cpu().numpy(), down.float().cpu().numpy(), up.float().cpu().numpy(),

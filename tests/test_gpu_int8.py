@@ -184,6 +184,7 @@ def test_int4_linear_unpacked_equals_packed(ck, m, k, n, bias_dtype):
 def test_public_linear_takes_unpacked_path_for_many_tokens(ck):
     import _int4
     from _int4 import weight_cache
+    was = weight_cache.enabled()
     weight_cache.enable(True)
     x = activation(512, 3072, 1)
     w = (torch.randn(1024, 3072) * 0.02).to(torch.float16).cuda()
@@ -193,7 +194,7 @@ def test_public_linear_takes_unpacked_path_for_many_tokens(ck):
     assert weight_cache.cached_bytes() == before + 1024 * 3072
     weight_cache.enable(False)
     y_packed = _int4.convrot_w4a4_linear(x, qw, ws)
-    weight_cache.enable(True)
+    weight_cache.enable(was)
     torch.cuda.synchronize()
     assert torch.equal(y, y_packed)
     ora = orc.convrot_w4a4_linear(bits(x), qw.cpu().numpy(), ws.cpu().numpy(), None, 256)
@@ -208,6 +209,7 @@ def test_public_linear_few_rows_dispatch(ck, m, k, n, unpacked):
     path, others stay packed; the output bits are the packed path's either way."""
     import _int4
     from _int4 import weight_cache
+    was = weight_cache.enabled()
     weight_cache.enable(True)
     x = activation(m, k, m + n)
     w = (torch.randn(n, k) * 0.02).to(torch.float16).cuda()
@@ -217,6 +219,6 @@ def test_public_linear_few_rows_dispatch(ck, m, k, n, unpacked):
     assert weight_cache.cached_bytes() == before + (n * k if unpacked else 0)
     weight_cache.enable(False)
     y_packed = _int4.convrot_w4a4_linear(x, qw, ws)
-    weight_cache.enable(True)
+    weight_cache.enable(was)
     torch.cuda.synchronize()
     assert torch.equal(y, y_packed)

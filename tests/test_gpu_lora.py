@@ -147,8 +147,11 @@ def test_int8_lora_on_unpacked_codes_equals_packed(ck, m, n, k, r, out_dtype):
 
 
 def test_public_lora_linear_many_tokens_takes_unpacked_path(ck):
+    """With the opt-in cache the LoRA linear runs on unpacked weights; without it,
+    the A8 form on the packed weights: the same bits."""
     import _int4
     from _int4 import weight_cache
+    was = weight_cache.enabled()
     weight_cache.enable(True)
     g = torch.Generator().manual_seed(3)
     x = torch.randn(512, 3072, generator=g).to(torch.bfloat16).cuda()
@@ -160,7 +163,7 @@ def test_public_lora_linear_many_tokens_takes_unpacked_path(ck):
     assert weight_cache.cached_bytes() == before + 1024 * 3072
     weight_cache.enable(False)
     y_packed = _int4.convrot_w4a4_linear_lora(x, qw, ws, None, ad)
-    weight_cache.enable(True)
+    weight_cache.enable(was)
     torch.cuda.synchronize()
     assert torch.equal(y, y_packed)
 

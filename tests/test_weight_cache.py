@@ -1,9 +1,18 @@
 """Host logic of the unpacked-weight cache (no GPU: a counting fake unpacker)."""
 import gc
 
+import pytest
 import torch
 
 from _int4 import weight_cache
+
+
+@pytest.fixture(autouse=True)
+def restore_cache_state():
+    """The cache is opt-in: every test here leaves it as it found it."""
+    was = weight_cache.enabled()
+    yield
+    weight_cache.enable(was)
 
 
 class CountingUnpack:
