@@ -484,7 +484,10 @@ convrot_quant_kernel(const T* __restrict__ x, int8_t* __restrict__ qout, float* 
 // 192 + rint(t) exactly (unit spacing in [128, 256), ties to even), whose low
 // mantissa nibble is the two's-complement code.
 
-constexpr int kQ5MaxThreads = 384;
+#ifndef CONVROT_Q5_MAX_THREADS
+#define CONVROT_Q5_MAX_THREADS 384
+#endif
+constexpr int kQ5MaxThreads = CONVROT_Q5_MAX_THREADS;
 constexpr int kQ5MaxTiles = kQ5MaxThreads / 2;           // tiles per round, at most
 #ifndef CONVROT_Q5_ROUND_TILES
 #define CONVROT_Q5_ROUND_TILES 48
@@ -519,8 +522,11 @@ __device__ __forceinline__ uint32_t bf16x2_add(uint32_t a, uint32_t b) {
 // sign-extended int8 per code [M, K] (the operand form of the int8 tensor-core
 // GEMM); BITS = 8: int8 codes [M, K] (scale = absmax / 127, the W8A8 tier,
 // _int4/int8_eager.py:22-27).
+#ifndef CONVROT_Q5_MIN_BLOCKS
+#define CONVROT_Q5_MIN_BLOCKS 1
+#endif
 template <int G, int BITS, bool UNPACKED = false>
-__global__ void __launch_bounds__(kQ5MaxThreads, 1)
+__global__ void __launch_bounds__(kQ5MaxThreads, CONVROT_Q5_MIN_BLOCKS)
 convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restrict__ qout,
                           float* __restrict__ scaleout, int M, int K, int rows_per_round) {
     static_assert(G == 64 || G == 256, "two-digit tiles only");
@@ -691,10 +697,10 @@ convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restric
                     }
                 }
             } else if constexpr (BITS == 4) {
-                // unpacked int4: the packed path's nibble (magic add of 192), sign
-                // extended within each 16-bit half, (n ^ 8) + 0xF8 = n - 8 mod 256
-                // in the low byte -- so the codes are those of the packed path for
-                // every input -- then one int8 per column, rows in order.
+                // unpacked int4: the packed path's magic add of 192 gives bf16 bits
+                // 0x4340 + q, whose low byte is 0x40 + q; subtracting 0x40 per 16-bit
+                // half leaves q sign-extended in the low byte -- so the codes are those
+                // of the packed path for every input -- then one int8 per column.
                 const uint32_t magic = 0x43404340u;
                 int8_t* dst = qout + static_cast<size_t>(row0 + my_row) * K + tile_in_row * 256 + hs * 128;
                 #pragma unroll
@@ -711,7 +717,7 @@ convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restric
                             for (int u = 0; u < 2; ++u) {
                                 const uint32_t y = packed[p][2 * jj + u];
                                 const float2 q = mul2(make_float2(__uint_as_float(y << 16), __uint_as_float(y & 0xFFFF0000u)), rcp2);
-                                c[u] = ((bf16x2_add(bf16x2_bits(q.x, q.y), magic) & 0x000F000Fu) ^ 0x00080008u) + 0x00F800F8u;
+                                c[u] = bf16x2_add(bf16x2_bits(q.x, q.y), magic) - 0x00400040u;
                             }
                             pr[jj] = __byte_perm(c[0], c[1], 0x6240);
                         }
