@@ -147,8 +147,9 @@ def convrot_w4a4_linear(
 
 _MAX_LORA_RANK = 64
 # Unit roundoff of the side path's operand type (T = x.A^T and B enter the
-# tensor cores in bf16): the bound a caller's tolerance on the LoRA term needs.
-LORA_OPERAND_UNIT = 2.0 ** -8
+# tensor cores in fp16, the reference's adapter dtype, int4_ops.py:165-167): the
+# bound a caller's tolerance on the LoRA term needs.
+LORA_OPERAND_UNIT = 2.0 ** -11
 
 
 def convrot_w4a4_linear_lora(
@@ -163,10 +164,14 @@ def convrot_w4a4_linear_lora(
 
     adapters: iterable of (down [r, K], up [N, r], scale) with scale = (alpha / r) * strength,
     the low-rank "bypass" of the node's forward (int4_ops.py:181-192). The down
-    projection T = x @ down^T runs as one bf16 GEMM; the up projection and the add
-    run on the tensor cores inside the int4 GEMM, before the single output
-    rounding. Several adapters are stacked along the rank (total rank <= 64); with
-    more than one, each scale is folded into its up matrix in bf16.
+    projection T = x @ down^T runs as one fp16 GEMM; the up projection and the add
+    run on fp16 tensor-core MMAs inside the int4 GEMM, fp32 accumulation, added
+    before the single output rounding (the reference adds the adapter's output to
+    the already rounded int4 output, int4_ops.py:183-192; one rounding is the
+    more accurate of the two and a deliberate difference). The adapters are in
+    fp16, as the reference prepares them (int4_ops.py:165-167). Several adapters
+    are stacked along the rank (total rank <= 64); with more than one, each scale
+    is folded into its up matrix in fp16.
     """
     adapters = list(adapters)
     if not adapters:
@@ -192,16 +197,16 @@ def convrot_w4a4_linear_lora(
 
 
 def _lora_operands(x2d: torch.Tensor, adapters, n: int):
-    """(T = x @ down^T [M, r] bf16, up [N, r] bf16, scale) for the fused side path;
+    """(T = x @ down^T [M, r] fp16, up [N, r] fp16, scale) for the fused side path;
     several adapters are stacked along the rank, each scale folded into its up
-    matrix in bf16; the rank is padded to a multiple of 8."""
+    matrix in fp16; the rank is padded to a multiple of 8."""
     if len(adapters) == 1:
         down, up, scale = adapters[0]
-        down = down.to(device=x2d.device, dtype=torch.bfloat16)
-        up = up.to(device=x2d.device, dtype=torch.bfloat16)
+        down = down.to(device=x2d.device, dtype=torch.float16)
+        up = up.to(device=x2d.device, dtype=torch.float16)
     else:
-        down = torch.cat([d.to(device=x2d.device, dtype=torch.bfloat16) for d, _, _ in adapters], dim=0)
-        up = torch.cat([(u.to(device=x2d.device, dtype=torch.float32) * float(s)).to(torch.bfloat16)
+        down = torch.cat([d.to(device=x2d.device, dtype=torch.float16) for d, _, _ in adapters], dim=0)
+        up = torch.cat([(u.to(device=x2d.device, dtype=torch.float32) * float(s)).to(torch.float16)
                         for _, u, s in adapters], dim=1)
         scale = 1.0
     rank = down.shape[0]
@@ -212,7 +217,7 @@ def _lora_operands(x2d: torch.Tensor, adapters, n: int):
     if pad:
         down = torch.nn.functional.pad(down, (0, 0, 0, pad))
         up = torch.nn.functional.pad(up, (0, pad))
-    return x2d.to(torch.bfloat16) @ down.t(), up, scale
+    return x2d.to(torch.float16) @ down.t(), up, scale
 
 
 def convrot_w8a8_linear(

@@ -160,7 +160,7 @@ def int4_convrot_gemm(x_packed, w_packed, x_scale, w_scale, bias, out_dtype):
 def int4_convrot_gemm_lora(x_packed, w_packed, x_scale, w_scale, bias, out_dtype, lora_t, lora_b, lora_scale):
     """int4_convrot_gemm plus lora_scale * (lora_t @ lora_b^T), fused in the epilogue.
 
-    lora_t: bf16 [M, r] (= x @ A^T), lora_b: bf16 [N, r], r a multiple of 8 up to 64.
+    lora_t: fp16 [M, r] (= x @ A^T), lora_b: fp16 [N, r], r a multiple of 8 up to 64.
     """
     x_packed, w_packed, m, n, k = _packed_pair(x_packed, w_packed)
     return _gemm_lora("ck_int4_convrot_gemm_lora", x_packed, w_packed, m, n, k, x_scale, w_scale, bias,
@@ -180,8 +180,8 @@ def _gemm_lora(name, xq, wq, m, n, k, x_scale, w_scale, bias, out_dtype, lora_t,
     if out_dtype not in _OUT_DTYPE_CODE:
         raise ValueError(f"LoRA gemm output dtype must be float32/bfloat16, got {out_dtype}")
     _require_cuda(lora_t, lora_b)
-    lora_t = lora_t.to(torch.bfloat16).contiguous()
-    lora_b = lora_b.to(torch.bfloat16).contiguous()
+    lora_t = lora_t.to(torch.float16).contiguous()
+    lora_b = lora_b.to(torch.float16).contiguous()
     r = lora_t.shape[1]
     if tuple(lora_t.shape) != (m, r) or tuple(lora_b.shape) != (n, r):
         raise ValueError(f"LoRA shapes {tuple(lora_t.shape)} / {tuple(lora_b.shape)} do not match M={m}, N={n}")
@@ -201,7 +201,7 @@ def int4_convrot_gemm_a8(x_codes, w_packed, x_scale, w_scale, bias, out_dtype,
     """The int4 GEMM on int8 activation codes [M, K] (one sign-extended code per byte,
     from convrot_quant_int4_unpacked) and packed int4 weights [N, K/2]: the same
     accumulators and output bits as int4_convrot_gemm on the packed codes. With
-    lora_t / lora_b (bf16 [M, r] / [N, r]) the Dynamic-LoRA side path is fused as in
+    lora_t / lora_b (fp16 [M, r] / [N, r]) the Dynamic-LoRA side path is fused as in
     int4_convrot_gemm_lora. out_dtype torch.int32 returns the exact accumulators."""
     lib = _load()
     _require_cuda(x_codes, w_packed, x_scale, w_scale)
@@ -221,8 +221,8 @@ def int4_convrot_gemm_a8(x_codes, w_packed, x_scale, w_scale, bias, out_dtype,
     r = 0
     if lora_t is not None:
         _require_cuda(lora_t, lora_b)
-        lora_t = lora_t.to(torch.bfloat16).contiguous()
-        lora_b = lora_b.to(torch.bfloat16).contiguous()
+        lora_t = lora_t.to(torch.float16).contiguous()
+        lora_b = lora_b.to(torch.float16).contiguous()
         r = lora_t.shape[1]
         if tuple(lora_t.shape) != (m, r) or tuple(lora_b.shape) != (n, r):
             raise ValueError(f"LoRA shapes {tuple(lora_t.shape)} / {tuple(lora_b.shape)} do not match M={m}, N={n}")

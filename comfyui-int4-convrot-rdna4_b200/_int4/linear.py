@@ -93,7 +93,7 @@ class Int4ConvRotLinear(torch.nn.Module):
         prepared = []
         for down, up, alpha, strength in adapters:
             r = down.shape[0]
-            prepared.append((down.to(self._q.device, torch.bfloat16), up.to(self._q.device, torch.bfloat16),
+            prepared.append((down.to(self._q.device, torch.float16), up.to(self._q.device, torch.float16),
                              float(alpha) / r * float(strength)))
         self._dyn_lora = prepared
 

@@ -6,9 +6,12 @@ output columns for all tokens and an all-gather assembles [..., N] on every
 rank. The reference is single-device; this is the B200 build's column-parallel
 variant for the largest layers.
 
-On CUDA tensors the tokens go in row blocks: block i's all-gather (NCCL over
-NVLink, on a side stream) and its placement into the [M, N] output run while
-block i+1's columns are computed, so the exchange hides behind the GEMMs.
+With ``chunks`` > 1 (CUDA tensors) the tokens go in row blocks: block i's
+all-gather (NCCL over NVLink, on a side stream) and its placement into the
+[M, N] output run while block i+1's columns are computed. The default is one
+block: the local GEMM is persistent over every SM, so an all-gather running
+beside it takes SMs from it, and the overlapped form measured slower than
+computing all local columns first and gathering once.
 """
 from __future__ import annotations
 
@@ -44,7 +47,7 @@ def shard_adapters(adapters, rank: int, world: int):
 
 def _row_blocks(m: int, world: int, chunks: int | None):
     if chunks is None:
-        chunks = 4 if world <= 2 else 2
+        chunks = 1
     step = max(_ROW_ALIGN, ((m + chunks - 1) // chunks + _ROW_ALIGN - 1) // _ROW_ALIGN * _ROW_ALIGN)
     return [(lo, min(m, lo + step)) for lo in range(0, m, step)]
 
@@ -65,7 +68,7 @@ def _nsplit(x: torch.Tensor, local_fn, nl: int, group, chunks):
     lead = x.shape[:-1]
     x2d = x.reshape(-1, x.shape[-1])
     m = x2d.shape[0]
-    if not x.is_cuda or m == 0:
+    if not x.is_cuda or m == 0 or len(_row_blocks(m, world, chunks)) == 1:
         local = local_fn(x2d).contiguous()
         out = torch.empty((m, world * nl), dtype=local.dtype, device=local.device)
         _gather_into(out, local, world, group)

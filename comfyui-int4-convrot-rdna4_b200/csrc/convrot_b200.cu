@@ -1123,22 +1123,22 @@ bool make_out_tmap(CUtensorMap* map, void* out, int M, int N) {
                CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// bf16 matrix [rows, cols] (row-major) read in boxes of 64 columns x box_rows, 128 B swizzle.
-bool make_bf16_tmap(CUtensorMap* map, const void* base, int rows, int cols, int box_rows) {
+// fp16 matrix [rows, cols] (row-major) read in boxes of 64 columns x box_rows, 128 B swizzle.
+bool make_f16_tmap(CUtensorMap* map, const void* base, int rows, int cols, int box_rows) {
     auto enc = get_encode_fn();
     if (!enc) return false;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
     const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
     const cuuint32_t estr[2] = {1, 1};
-    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 struct LoraArgs {
-    const void* t = nullptr;      // bf16 [M, rank]
-    const void* b = nullptr;      // bf16 [N, rank]
+    const void* t = nullptr;      // fp16 [M, rank]
+    const void* b = nullptr;      // fp16 [N, rank]
     int rank = 0;
     float scale = 0.0f;
 };
@@ -1167,8 +1167,8 @@ int launch_pair_impl(const void* Xp, const void* Wp, const float* xs, const floa
         return fail("cuTensorMapEncodeTiled failed (pointer not 16-byte aligned or driver entry point missing)");
     if (STAGED && !make_out_tmap(&to, out, M, N))
         return fail("cuTensorMapEncodeTiled failed for the output");
-    if (LORA && (!make_bf16_tmap(&tlt, lora.t, M, lora.rank, 128) ||
-                 !make_bf16_tmap(&tlb, lora.b, N, lora.rank, BN / 2)))
+    if (LORA && (!make_f16_tmap(&tlt, lora.t, M, lora.rank, 128) ||
+                 !make_f16_tmap(&tlb, lora.b, N, lora.rank, BN / 2)))
         return fail("cuTensorMapEncodeTiled failed for the LoRA operands");
     auto kernel = int4_gemm_pair_kernel<BN, SWAP, OUT, STAGED, LORA, I8, A8>;
     cudaError_t e = ensure_smem(kernel, Cfg::kSmemBytes);

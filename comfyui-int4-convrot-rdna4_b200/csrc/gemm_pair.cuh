@@ -105,7 +105,7 @@ struct PairCfg {
     // bf16 output tile staged for the TMA store: 128 rows x BN cols, 64-col boxes
     static constexpr int kStagingBytes = STAGED ? 128 * BN * 2 : 0;
     // 227 KB per block, minus alignment slack, barriers and the staging tile
-    // Dynamic-LoRA operands per tile: T rows (x A^T, bf16, 64 per 128 B row) and
+    // Dynamic-LoRA operands per tile: T rows (x A^T, fp16, 64 per 128 B row) and
     // this CTA's half of the LoRA up-projection rows
     static constexpr int kLoraTBytes = LORA ? 128 * 128 : 0;
     static constexpr int kLoraBBytes = LORA ? kBHalf * 128 : 0;
@@ -142,7 +142,7 @@ struct PairCfg {
     static constexpr int kColOffset = kMiscOffset + 16;
     static constexpr int kSmemBytes = kColOffset + 2 * 2 * BN * 4 + 1024;
     static constexpr uint32_t kIdesc = idesc_i8(256, BN);
-    static constexpr uint32_t kIdescLora = idesc_bf16(256, BN);
+    static constexpr uint32_t kIdescLora = idesc_f16(256, BN);    // fp16 T and B, fp32 accumulator
     // swapped (weight-bound) tiles: three groups of four warps take turns on
     // whole stages (A and B), otherwise four A and four B expander warps
     static constexpr int kExpGroups = SWAP ? 3 : 1;
@@ -212,7 +212,7 @@ __device__ __forceinline__ void store_row32(void* out, size_t obase, int n, int 
 // STAGED (bf16, not swapped, N % 8 == 0): output goes through a shared-memory
 // tile and TMA stores (tmap_out); otherwise the epilogue stores directly.
 // LORA (not swapped): a rank <= 64 side path out += lora_scale * T[m, :] . B[n, :]
-// (T = x A^T precomputed, both bf16) on the tensor cores into a second, fp32
+// (T = x A^T precomputed, both fp16) on the tensor cores into a second, fp32
 // accumulator, added in the epilogue before the single output rounding.
 template <int BN, bool SWAP, int OUT, bool STAGED, bool LORA = false, bool I8 = false, bool A8 = false>
 __global__ void __launch_bounds__(kPairThreads, 1)
@@ -390,7 +390,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                 const uint32_t acc_tmem = tmem_base + abuf * Cfg::kAccCols;
                 tc_fence_after();
                 if constexpr (LORA) {
-                    // the side path T . B^T on bf16 MMAs into this buffer's fp32 half, ahead
+                    // the side path T . B^T on fp16 MMAs into this buffer's fp32 half, ahead
                     // of the K loop: its operand slot is then free for the next tile's
                     // side path early, and the producer does not stall between tiles
                     if (ok && !__all_sync(0xFFFFFFFFu, mbar_wait_bounded(lora_full_bar, lt & 1))) {
@@ -404,7 +404,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                         if (elect_one()) {
                             #pragma unroll
                             for (int j = 0; j < 4; ++j)    // rank 64 = four K = 16 bf16 steps of a 128 B row
-                                mma_bf16_ss_pair(tmem_lora(abuf), dt + 2 * j, dl + 2 * j, Cfg::kIdescLora, j != 0);
+                                mma_f16kind_ss_pair(tmem_lora(abuf), dt + 2 * j, dl + 2 * j, Cfg::kIdescLora, j != 0);
                             mma_commit_pair_multicast(lora_empty_bar, 0x3);
                         }
                         __syncwarp();
@@ -475,7 +475,7 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                         const uint32_t t_addr = smem_u32(lora_t), b_addr = smem_u32(lora_b);
                         #pragma unroll
                         for (int j = 0; j < 4; ++j)        // rank 64 = four K = 16 bf16 steps of a 128 B row
-                            mma_bf16_ss_pair(tmem_lora(abuf), smem_desc_kmajor(t_addr + 32 * j, 1024, kSwizzle128),
+                            mma_f16kind_ss_pair(tmem_lora(abuf), smem_desc_kmajor(t_addr + 32 * j, 1024, kSwizzle128),
                                              smem_desc_kmajor(b_addr + 32 * j, 1024, kSwizzle128),
                                              Cfg::kIdescLora, j != 0);
                         mma_commit_pair_multicast(lora_empty_bar, 0x3);

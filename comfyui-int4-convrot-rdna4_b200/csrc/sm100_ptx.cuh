@@ -332,7 +332,7 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 namespace convrot {
 
 // Pair MMA, both operands from shared memory, bf16 inputs, fp32 accumulator.
-__device__ __forceinline__ void mma_bf16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+__device__ __forceinline__ void mma_f16kind_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                                  uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -343,6 +343,13 @@ __device__ __forceinline__ void mma_bf16_ss_pair(uint32_t d_tmem, uint64_t a_des
 }
 
 // Instruction descriptor for kind::f16 with bf16 A and B (K-major) and an fp32 accumulator.
+// (kind::f16 MMAs with either descriptor use mma_f16kind_ss_pair.)
+// kind::f16 with fp16 A and B (the Dynamic-LoRA side path), fp32 D
+__host__ __device__ constexpr uint32_t idesc_f16(uint32_t m, uint32_t n) {
+    return (1u << 4)            // D format: F32
+         | ((n >> 3) << 17)     // A, B: f16 (format 0)
+         | ((m >> 4) << 24);
+}
 __host__ __device__ constexpr uint32_t idesc_bf16(uint32_t m, uint32_t n) {
     return (1u << 4)            // D format: F32
          | (1u << 7)            // A: bf16

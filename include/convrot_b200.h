@@ -109,8 +109,9 @@ int ck_convrot_w4a4_linear_noalloc(const void* x, int in_dtype, const void* Wp, 
 
 /* ck_int4_convrot_gemm plus a fused Dynamic-LoRA side path:
  *   out[m, n] = (((float(D) * xscale[m]) * wscale[n]) + bias[n]) + lora_scale * L[m, n],
- *   L = lora_t[m, :] . lora_b[n, :]  (bf16 operands, fp32 tensor-core accumulation).
- * lora_t = x A^T [M, rank] and lora_b = B [N, rank] are bf16 row-major; rank a
+ *   L = lora_t[m, :] . lora_b[n, :]  (fp16 operands, fp32 tensor-core accumulation).
+ * lora_t = x A^T [M, rank] and lora_b = B [N, rank] are fp16 row-major (the
+ * reference's adapter dtype, int4_ops.py:165-167); rank a
  * multiple of 8 in [8, 64]; bias in bias_dtype as for ck_convrot_w4a4_linear.
  * Replaces the unfused per-adapter `out + v.h(x, out)`
  * of the node's forward (int4_ops.py:181-192, :383); no HIP export counterpart. */
@@ -178,7 +179,7 @@ int ck_int8_gemm_s32(const void* X, const void* W, void* acc, int M, int N, int 
  *   out [M, N], out_dtype 0 = f32, 1 = bf16, 3 = int32 exact accumulators D
  *   (scales and bias ignored); K % 128 == 0, K <= 65536.
  * Optional Dynamic-LoRA side path as ck_int4_convrot_gemm_lora (lora_t, lora_b
- * bf16 [M, rank] / [N, rank], rank a multiple of 8 in [8, 64]; both NULL: none).
+ * fp16 [M, rank] / [N, rank], rank a multiple of 8 in [8, 64]; both NULL: none).
  * The weights stay packed in HBM and are expanded in shared memory; the
  * activations go to the tensor cores as loaded. Same D, epilogue and output
  * bits as the packed-code GEMM. */

@@ -94,8 +94,8 @@ def test_a8_lora_equals_packed_lora(ck, m, n, k, r, out_dtype):
     """Same side-path operands and MMAs as the packed LoRA GEMM: the same bits."""
     codes, xp, wp, xs, ws, bias = operands(m, n, k, m + r)
     g = torch.Generator().manual_seed(r)
-    lt = (torch.randn(m, r, generator=g) * 0.5).to(torch.bfloat16).cuda()
-    lb = (torch.randn(n, r, generator=g) * 0.01).to(torch.bfloat16).cuda()
+    lt = (torch.randn(m, r, generator=g) * 0.5).to(torch.float16).cuda()
+    lb = (torch.randn(n, r, generator=g) * 0.01).to(torch.float16).cuda()
     a = ck.int4_convrot_gemm_a8(codes, wp, xs, ws, bias, out_dtype, lt, lb, 0.75)
     b = ck.int4_convrot_gemm_lora(xp, wp, xs, ws, bias, out_dtype, lt, lb, 0.75)
     torch.cuda.synchronize()

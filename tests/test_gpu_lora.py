@@ -3,7 +3,9 @@
 The side path's arithmetic belongs to ComfyUI's LoRA adapter, which the
 reference does not vendor (int4_ops.py:181-192 calls ``v.h(x, out)``), so it has
 no pinned golden vectors; it is checked against the oracle's definition
-(oracle.int4_gemm_epilogue_lora) and against a plain fp32 torch reference.
+(oracle.int4_gemm_epilogue_lora) and against a plain fp32 torch reference. Its
+operands are fp16, the dtype the reference prepares adapters in
+(int4_ops.py:165-167).
 
 Tolerance: the tensor cores accumulate L = T . B^T in fp32 in an unspecified
 order, so the fused output may differ from the oracle by at most one unit in the
@@ -53,8 +55,8 @@ def test_fused_lora_epilogue_vs_oracle(ck, m, n, k, r, out_dtype):
     xs = (torch.rand(m, generator=g) * 0.05 + 1e-3).cuda()
     ws = (torch.rand(n, generator=g) * 0.01 + 1e-4).cuda()
     bias = (torch.randn(n, generator=g) * 0.01).cuda()
-    lt = (torch.randn(m, r, generator=g) * 0.5).to(torch.bfloat16).cuda()
-    lb = (torch.randn(n, r, generator=g) * 0.01).to(torch.bfloat16).cuda()
+    lt = (torch.randn(m, r, generator=g) * 0.5).to(torch.float16).cuda()
+    lb = (torch.randn(n, r, generator=g) * 0.01).to(torch.float16).cuda()
     scale = 0.75
     out = ck.int4_convrot_gemm_lora(xp, wp, xs, ws, bias, out_dtype, lt, lb, scale)
     torch.cuda.synchronize()
@@ -81,8 +83,8 @@ def test_fused_lora_zero_side_path_matches_plain_gemm(ck):
     xs = torch.rand(m, generator=g).cuda()
     ws = torch.rand(n, generator=g).cuda() * 0.01
     bias = torch.randn(n, generator=g).cuda() * 0.01
-    lt = torch.randn(m, r, generator=g).to(torch.bfloat16).cuda()
-    lb = torch.zeros(n, r, dtype=torch.bfloat16, device="cuda")
+    lt = torch.randn(m, r, generator=g).to(torch.float16).cuda()
+    lb = torch.zeros(n, r, dtype=torch.float16, device="cuda")
     a = ck.int4_convrot_gemm_lora(xp, wp, xs, ws, bias, torch.bfloat16, lt, lb, 1.0)
     b = ck.int4_convrot_gemm(xp, wp, xs, ws, bias, torch.bfloat16)
     torch.cuda.synchronize()
@@ -115,8 +117,8 @@ def test_lora_rejects_bad_rank(ck):
     xp = torch.zeros(m, k // 2, dtype=torch.int8, device="cuda")
     wp = torch.zeros(n, k // 2, dtype=torch.int8, device="cuda")
     s = torch.ones(max(m, n), device="cuda")
-    lt = torch.zeros(m, 72, dtype=torch.bfloat16, device="cuda")
-    lb = torch.zeros(n, 72, dtype=torch.bfloat16, device="cuda")
+    lt = torch.zeros(m, 72, dtype=torch.float16, device="cuda")
+    lb = torch.zeros(n, 72, dtype=torch.float16, device="cuda")
     with pytest.raises(RuntimeError, match="rank"):
         ck.int4_convrot_gemm_lora(xp, wp, s[:m], s[:n], None, torch.bfloat16, lt, lb, 1.0)
 
@@ -138,8 +140,8 @@ def test_int8_lora_on_unpacked_codes_equals_packed(ck, m, n, k, r, out_dtype):
     xs = (torch.rand(m, generator=g) * 0.05 + 1e-3).cuda()
     ws = (torch.rand(n, generator=g) * 0.01 + 1e-4).cuda()
     bias = (torch.randn(n, generator=g) * 0.01).to(torch.float16).cuda()
-    lt = (torch.randn(m, r, generator=g) * 0.5).to(torch.bfloat16).cuda()
-    lb = (torch.randn(n, r, generator=g) * 0.01).to(torch.bfloat16).cuda()
+    lt = (torch.randn(m, r, generator=g) * 0.5).to(torch.float16).cuda()
+    lb = (torch.randn(n, r, generator=g) * 0.01).to(torch.float16).cuda()
     a = ck.int8_convrot_gemm_lora(ck.int4_unpack(xp), ck.int4_unpack(wp), xs, ws, bias, out_dtype, lt, lb, 0.75)
     b = ck.int4_convrot_gemm_lora(xp, wp, xs, ws, bias, out_dtype, lt, lb, 0.75)
     torch.cuda.synchronize()
