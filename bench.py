@@ -135,6 +135,16 @@ def load_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
+def load_traffic():
+    """Per-launch DRAM bytes (read + write) of the dominant GEMM, from the committed
+    summary of one ncu capture of it (profiles/roofline_traffic.json)."""
+    path = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    if not os.path.exists(path):
+        return {}
+    with open(path) as f:
+        return json.load(f)
+
+
 def synth_activation(m, k, gen, device):
     x = torch.randn(m, k, generator=gen)
     idx = torch.randperm(k, generator=gen)[: max(1, k // 100)]
@@ -500,7 +510,10 @@ def roofline_probes(layers, xs, device, flush, stream):
         "frac": achieved / int8_peak,
         "peak_source": f"2 x {peak_src} bf16 burst ({peaks['bf16_tflops']} TFLOP/s): B200 dense int8 rate",
         "ms_per_launch": gemm_ms,
-        "traffic": None,
+        "traffic": load_traffic().get({"a8": "a8_pair_bytes_per_launch", "unpacked": "int8_pair_unpacked_bytes_per_launch",
+                                       "packed": "int4_gemm_kernel_bytes_per_launch"}[form]),
+        "traffic_note": "ncu dram read + write of one launch at this shape; the output fits in L2, so part of "
+                        "its write-back lands after the kernel (profiles/a8_pair_mlp_up_m4608.md)",
         "algorithmic_bytes": (m * k + n * k) // 2 + 4 * m + 4 * n + 2 * n + 2 * m * n,
         "bytes_read_as_launched": int(code_bytes[0] * m * k + code_bytes[1] * n * k) + 4 * m + 4 * n + 2 * n
                                   + 2 * m * n,
@@ -939,6 +952,8 @@ def run_case(args):
         m, k, n = 1, 3072, 18432
     else:
         m, k, n = M_TOKENS, 3072, 12288
+    if args.m:
+        m = args.m
     w = (torch.randn(n, k, generator=gen) * 0.02).to(torch.float16).to(device)
     qw, ws = _int4.quantize_convrot_w4a4_weight(w, GROUP)
     bias = torch.zeros(n, device=device)
@@ -984,6 +999,7 @@ def main():
                     default=None,
                     help="run one kernel --iters times (profiling helper) instead of the benchmark")
     ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--m", type=int, default=0, help="token rows of the --case kernel (default: the case's own)")
     args = ap.parse_args()
     if args.case:
         run_case(args)
