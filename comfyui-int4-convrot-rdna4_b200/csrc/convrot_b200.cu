@@ -813,6 +813,7 @@ enum : int { kOutF32 = 0, kOutBF16 = 1, kOutF32Accumulate = 2, kOutS32 = 3 };
 }  // namespace convrot
 
 #include "gemm_pair.cuh"
+#include "gemm_a8t.cuh"
 
 namespace convrot {
 
@@ -1305,6 +1306,83 @@ int dispatch_gemm_i8(const void* X, const void* W, const float* xs, const float*
     return launch_pair_impl<256, false, OUT, false, false, true>(X, W, xs, ws, bias, out, M, N, K, LoraArgs(), stream);
 }
 
+// Packed int4 weights [rows, K/2] in boxes of 128 rows x 64 bytes (128 codes), 64-byte swizzle.
+bool make_w64_tmap(CUtensorMap* map, const void* base, int rows, int K) {
+    auto enc = get_encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K / 2), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K / 2)};
+    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// bf16 output [M, N] for TMA stores of 32-token x 32-column boxes (64 B rows, 64 B swizzle).
+bool make_out_box32_tmap(CUtensorMap* map, void* out, int M, int N) {
+    auto enc = get_encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(N) * 2};
+    const cuuint32_t box[2] = {32, 32};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+               CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The A8T form (weights as the TMEM operand): 256 weight rows x BN tokens per CTA pair.
+template <int BN, int OUT, bool STAGED>
+int launch_a8t_impl(const void* X8, const void* Wp, const float* xs, const float* ws, BiasRef bias, void* out,
+                    int M, int N, int K, cudaStream_t stream) {
+    using Cfg = A8tCfg<BN, STAGED>;
+    CUtensorMap tx, tw, to;
+    memset(&to, 0, sizeof(to));
+    if (!make_packed_tmap(&tx, X8, M, 2 * K, BN / 2) || !make_w64_tmap(&tw, Wp, N, K))
+        return fail("cuTensorMapEncodeTiled failed (pointer not 16-byte aligned or driver entry point missing)");
+    if (STAGED && !make_out_box32_tmap(&to, out, M, N)) return fail("cuTensorMapEncodeTiled failed for the output");
+    auto kernel = int4_gemm_a8t_kernel<BN, OUT, STAGED>;
+    cudaError_t e = ensure_smem(kernel, Cfg::kSmemBytes);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    const int tiles_w = (N + 255) / 256;
+    const long num_tiles = static_cast<long>(tiles_w) * ((M + BN - 1) / BN);
+    if (num_tiles > 0x7FFFFFFF) return fail("too many output tiles");
+    const int clusters = static_cast<int>(num_tiles < sm_count() / 2 ? num_tiles : sm_count() / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.blockDim = dim3(kPairThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    e = cudaLaunchKernelEx(&cfg, kernel, tx, tw, to, xs, ws, bias, out, M, N, K, tiles_w,
+                           static_cast<int>(num_tiles), Wp);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    return static_cast<int>(cudaGetLastError());
+}
+
+template <int BN, int OUT>
+int launch_a8t(const void* X8, const void* Wp, const float* xs, const float* ws, BiasRef bias, void* out,
+               int M, int N, int K, cudaStream_t stream) {
+    if constexpr (OUT == kOutBF16) {
+        if (N % 8 == 0 && aligned16(out))
+            return launch_a8t_impl<BN, OUT, true>(X8, Wp, xs, ws, bias, out, M, N, K, stream);
+    }
+    return launch_a8t_impl<BN, OUT, false>(X8, Wp, xs, ws, bias, out, M, N, K, stream);
+}
+
+#ifndef CONVROT_A8T_BN
+#define CONVROT_A8T_BN 256
+#endif
+
 // int4 layers on int8 activation codes and packed weights (the A8 form): 256 x 256
 // pair tiles, or 256 x 128 when 256-column tiles leave most CTA pairs idle; with
 // a LoRA side path the same rule (256-column LoRA tiles hold one accumulator pair).
@@ -1318,6 +1396,12 @@ int dispatch_gemm_a8(const void* X8, const void* Wp, const float* xs, const floa
                                                                                lora, stream);
         return launch_pair_impl<128, false, OUT, false, true, false, true>(X8, Wp, xs, ws, bias, out, M, N, K,
                                                                            lora, stream);
+    }
+    if (CONVROT_A8T_BN > 0) {
+        const long tiles_t = static_cast<long>((N + 255) / 256) * ((M + CONVROT_A8T_BN - 1) / CONVROT_A8T_BN);
+        if (2 * tiles_t >= sm_count())
+            return launch_a8t<(CONVROT_A8T_BN > 0 ? CONVROT_A8T_BN : 192), OUT>(X8, Wp, xs, ws, bias, out, M, N, K,
+                                                                               stream);
     }
     if (2 * tiles256 >= sm_count() / 2)
         return launch_pair_impl<256, false, OUT, false, false, false, true>(X8, Wp, xs, ws, bias, out, M, N, K,

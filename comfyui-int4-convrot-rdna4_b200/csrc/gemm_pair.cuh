@@ -226,8 +226,10 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
     static_assert(!LORA || !SWAP, "the LoRA side path is fused into non-swapped tiles");
     static_assert(!STAGED || (OUT == kOutBF16 && !SWAP), "staged epilogue is for bf16, non-swapped tiles");
     extern __shared__ __align__(1024) unsigned char psmem_raw[];
-    unsigned char* smem = reinterpret_cast<unsigned char*>(
-        (reinterpret_cast<uintptr_t>(psmem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    // 1024-byte aligned by pointer arithmetic on the shared array itself, so the
+    // compiler keeps the shared address space (ld.shared / st.shared, not generic
+    // accesses) for everything addressed from here
+    unsigned char* smem = psmem_raw + ((1024u - (smem_u32(psmem_raw) & 1023u)) & 1023u);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset);
     uint64_t* full_bar = bars;
     uint64_t* empty_bar = bars + Cfg::kStages;

@@ -5,6 +5,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cstring>
 #include <cuda_runtime.h>
 
 namespace convrot {
@@ -161,6 +162,66 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
         : "r"(taddr));
 }
 
+// Packed fp32 pairs (sm_100): component-wise round-to-nearest products and sums.
+// A chain of products equals the scalar __fmul_rn sequence bit for bit; a packed
+// sum fed by packed products was seen to differ from the scalar sequence on
+// rounding ties, so sums of products stay scalar (__fadd_rn).
+__device__ __forceinline__ float2 fmul2_rn(float2 a, float2 b) {
+    uint64_t ua, ub, r;
+    memcpy(&ua, &a, 8);
+    memcpy(&ub, &b, 8);
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(ua), "l"(ub));
+    float2 o;
+    memcpy(&o, &r, 8);
+    return o;
+}
+
+__device__ __forceinline__ float2 fadd2_rn(float2 a, float2 b) {
+    uint64_t ua, ub, r;
+    memcpy(&ua, &a, 8);
+    memcpy(&ub, &b, 8);
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(ua), "l"(ub));
+    float2 o;
+    memcpy(&o, &r, 8);
+    return o;
+}
+
+// 16 lanes x 32 consecutive 32-bit columns (16x256b shape, four 8-column
+// groups): thread t gets, for group j, r[4j] / r[4j+1] = lane t/4 at columns
+// 8j + 2(t%4) and +1, r[4j+2] / r[4j+3] = lane t/4 + 8 at the same columns.
+__device__ __forceinline__ void tmem_ld_16x256b_x4(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.16x256b.x4.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+// Four 8x8 b16 matrices from registers to shared memory, transposed: register i
+// of thread t holds row t/4, columns 2(t%4) and +1 of matrix i; thread t gives
+// the address of stored row t%8 of matrix t/8, which receives that matrix's
+// column t%8 (16 bytes).
+__device__ __forceinline__ void stmatrix_x4_trans(uint32_t saddr, uint32_t r0, uint32_t r1, uint32_t r2,
+                                                  uint32_t r3) {
+    asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};"
+                 :: "r"(saddr), "r"(r0), "r"(r1), "r"(r2), "r"(r3) : "memory");
+}
+
+// tcgen05.wait::ld that also ties the registers of the awaited load to the
+// wait, so no use of them can be scheduled before it (for loads left in
+// flight across other work).
+__device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                   "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+                   "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]),
+                   "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]),
+                   "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -305,6 +366,12 @@ __device__ __forceinline__ void bulk_commit_group() {
 // Wait until every committed bulk store has finished reading shared memory.
 __device__ __forceinline__ void bulk_wait_group_read0() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// Wait until all but the most recently committed bulk store group have finished
+// reading shared memory.
+__device__ __forceinline__ void bulk_wait_group_read1() {
+    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
 }
 
 // Wait until every committed bulk store has completed.

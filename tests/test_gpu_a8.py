@@ -77,6 +77,24 @@ def test_a8_output_equals_packed_gemm(ck, m, n, k, out_dtype, bias_dtype):
     assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("m,n,k", [(2000, 2004, 1024), (1500, 3001, 512), (4608, 3072, 3072), (777, 9000, 256)])
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32, torch.int32])
+def test_a8_many_tiles_ragged_equals_packed(ck, m, n, k, out_dtype):
+    """Shapes with enough tiles for the weights-in-TMEM form, with ragged token and
+    weight edges, N not a multiple of 8 (direct stores) and odd N."""
+    codes, xp, wp, xs, ws, bias = operands(m, n, k, m * 3 + n)
+    if out_dtype == torch.int32:
+        a = ck.int4_convrot_gemm_a8(codes, wp, torch.ones(m, device="cuda"), torch.ones(n, device="cuda"),
+                                    None, torch.int32)
+        b = ck.int4_gemm_s32(xp, wp)
+    else:
+        a = ck.int4_convrot_gemm_a8(codes, wp, xs, ws, bias, out_dtype)
+        b = ck.int4_convrot_gemm(xp, wp, xs, ws, bias, out_dtype)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    assert ck.device_status() == 0
+
+
 def test_a8_output_vs_oracle_epilogue(ck):
     m, n, k = 300, 520, 768
     codes, xp, wp, xs, ws, bias = operands(m, n, k, 17)
