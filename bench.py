@@ -490,7 +490,8 @@ def roofline_probes(layers, xs, device, flush, stream):
         quant = ck.convrot_quant_int4_unpacked
         xq, xsc = quant(x, GROUP)
         gemm = lambda: ck.int4_convrot_gemm_a8(xq, up["qw"], xsc, up["ws"], up["bias"], torch.bfloat16)
-        gemm_name, code_bytes, form = "A8 pair GEMM (int8 activation codes, packed int4 weights)", (1, 0.5), "a8"
+        gemm_name, code_bytes, form = ("A8T GEMM (int8 activation codes by TMA, packed int4 weights expanded into "
+                                       "tensor memory)", (1, 0.5), "a8")
     else:
         quant = ck.convrot_quant_int4
         xq, xsc = quant(x, GROUP)
@@ -505,15 +506,16 @@ def roofline_probes(layers, xs, device, flush, stream):
     int8_peak = 2.0 * peaks["bf16_tflops"]           # dense int8 rate = 2x bf16 on B200
     achieved = gemm_ops / (gemm_ms * 1e-3) / 1e12
     extras["roofline"] = {
-        "kernel": f"int4_gemm_pair_kernel, {gemm_name} (MLP up 3072->12288, M=4608)",
+        "kernel": f"{'int4_gemm_a8t_kernel' if form == 'a8' else 'int4_gemm_pair_kernel'}, {gemm_name} "
+                  f"(MLP up 3072->12288, M=4608)",
         "bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS",
         "frac": achieved / int8_peak,
         "peak_source": f"2 x {peak_src} bf16 burst ({peaks['bf16_tflops']} TFLOP/s): B200 dense int8 rate",
         "ms_per_launch": gemm_ms,
-        "traffic": load_traffic().get({"a8": "a8_pair_bytes_per_launch", "unpacked": "int8_pair_unpacked_bytes_per_launch",
+        "traffic": load_traffic().get({"a8": "a8t_bytes_per_launch", "unpacked": "int8_pair_unpacked_bytes_per_launch",
                                        "packed": "int4_gemm_kernel_bytes_per_launch"}[form]),
         "traffic_note": "ncu dram read + write of one launch at this shape; the output fits in L2, so part of "
-                        "its write-back lands after the kernel (profiles/a8_pair_mlp_up_m4608.md)",
+                        "its write-back lands after the kernel (profiles/a8t_mlp_up_m4608.md)",
         "algorithmic_bytes": (m * k + n * k) // 2 + 4 * m + 4 * n + 2 * n + 2 * m * n,
         "bytes_read_as_launched": int(code_bytes[0] * m * k + code_bytes[1] * n * k) + 4 * m + 4 * n + 2 * n
                                   + 2 * m * n,
