@@ -164,7 +164,8 @@ def convrot_w4a4_linear_lora(
 
     adapters: iterable of (down [r, K], up [N, r], scale) with scale = (alpha / r) * strength,
     the low-rank "bypass" of the node's forward (int4_ops.py:181-192). The down
-    projection T = x @ down^T runs as one fp16 GEMM; the up projection and the add
+    projection T = fp16(x) @ down^T runs on the tensor cores (ck_lora_down: x read
+    once, converted to fp16 in shared memory, fp32 accumulation); the up projection and the add
     run on fp16 tensor-core MMAs inside the int4 GEMM, fp32 accumulation, added
     before the single output rounding (the reference adds the adapter's output to
     the already rounded int4 output, int4_ops.py:183-192; one rounding is the
@@ -197,7 +198,7 @@ def convrot_w4a4_linear_lora(
 
 
 def _lora_operands(x2d: torch.Tensor, adapters, n: int):
-    """(T = x @ down^T [M, r] fp16, up [N, r] fp16, scale) for the fused side path;
+    """(T = fp16(x) @ down^T [M, r] fp16, up [N, r] fp16, scale) for the fused side path;
     several adapters are stacked along the rank, each scale folded into its up
     matrix in fp16; the rank is padded to a multiple of 8."""
     if len(adapters) == 1:
@@ -217,7 +218,7 @@ def _lora_operands(x2d: torch.Tensor, adapters, n: int):
     if pad:
         down = torch.nn.functional.pad(down, (0, 0, 0, pad))
         up = torch.nn.functional.pad(up, (0, pad))
-    return x2d.to(torch.float16) @ down.t(), up, scale
+    return cuda_loader.lora_down(x2d, down), up, scale
 
 
 def convrot_w8a8_linear(

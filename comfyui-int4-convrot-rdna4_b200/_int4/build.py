@@ -14,7 +14,7 @@ import subprocess
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _CSRC = os.path.join(os.path.dirname(_HERE), "csrc")
 SOURCES = ["convrot_b200.cu", "noalloc.cu"]
-HEADERS = ["sm100_ptx.cuh", "gemm_pair.cuh", "linear_api.cuh"]
+HEADERS = ["sm100_ptx.cuh", "gemm_pair.cuh", "gemm_a8t.cuh", "lora_down.cuh", "linear_api.cuh"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

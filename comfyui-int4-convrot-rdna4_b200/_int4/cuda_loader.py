@@ -38,6 +38,7 @@ _SIGNATURES = {
     "ck_int8_gemm_s32": [_P, _P, _P, _I, _I, _I, _P],
     "ck_int8_convrot_gemm_lora": [_P] * 5 + [_I, _P] + [_I] * 4 + [_P, _P, _I, ctypes.c_float, _P],
     "ck_int4_unpack": [_P, _P, ctypes.c_longlong, _I, _P],
+    "ck_lora_down": [_P, _I, _P, _P, _I, _I, _I, _P],
     "ck_int4_convrot_gemm_a8": [_P] * 5 + [_I, _P] + [_I] * 4 + [_P, _P, _I, ctypes.c_float, _P],
     "ck_convrot_quant_int4_unpacked": [_P, _I, _P, _P, _I, _I, _I, _P],
     "ck_convrot_w4a4_linear_unpacked_workspace_size": [_I, _I],
@@ -426,6 +427,28 @@ def int8_gemm_s32(x_int8, w_int8):
     rc = lib.ck_int8_gemm_s32(x_int8.data_ptr(), w_int8.data_ptr(), acc.data_ptr(), m, n, k, _stream(x_int8))
     _check("ck_int8_gemm_s32", rc)
     return acc
+
+
+# --------------------------------------------------------------------- Dynamic-LoRA down projection
+
+
+def lora_down(x: torch.Tensor, down: torch.Tensor) -> torch.Tensor:
+    """T = fp16(x) @ down^T as fp16 [M, R] on the tensor cores (ck_lora_down).
+
+    x [M, K] bf16 or fp16 (f32 is cast to fp16 first), down [R, K] fp16 with R a
+    multiple of 8 in [8, 64]; fp32 accumulation, one rounding to fp16."""
+    lib = _load()
+    _require_cuda(x, down)
+    if x.dtype == torch.float32:
+        x = x.to(torch.float16)
+    x = x.contiguous()
+    down = down.to(torch.float16).contiguous()
+    m, k = x.shape
+    r = down.shape[0]
+    t = torch.empty((m, r), dtype=torch.float16, device=x.device)
+    rc = lib.ck_lora_down(x.data_ptr(), _IN_DTYPE_CODE[x.dtype], down.data_ptr(), t.data_ptr(), m, k, r, _stream(x))
+    _check("ck_lora_down", rc)
+    return t
 
 
 # --------------------------------------------------------------------- unpacked-code path

@@ -814,6 +814,7 @@ enum : int { kOutF32 = 0, kOutBF16 = 1, kOutF32Accumulate = 2, kOutS32 = 3 };
 
 #include "gemm_pair.cuh"
 #include "gemm_a8t.cuh"
+#include "lora_down.cuh"
 
 namespace convrot {
 
@@ -1562,6 +1563,46 @@ int run_linear(const void* x, int in_dtype, const void* Wp, const float* ws, Bia
     return dispatch_gemm<kOutF32>(q, Wp, xs, ws, bias, out, M, N, K, stream);
 }
 
+// Dynamic-LoRA down projection (lora_down.cuh): one 128-row tile per CTA, K split
+// over a cluster of up to 8 CTAs when the tiles alone would leave most SMs idle.
+template <bool kConvert>
+int launch_lora_down(const void* x, const void* down, void* t, int M, int K, int R, cudaStream_t stream) {
+    CUtensorMap tx, ta;
+    // the x map only moves 2-byte elements (no conversion in the copy), so bf16 x
+    // uses the fp16 map; out-of-bounds elements are zero bits in either type
+    if (!make_f16_tmap(&tx, x, M, K, kLdRows) || !make_f16_tmap(&ta, down, R, K, kLdN))
+        return fail("cuTensorMapEncodeTiled failed (pointer not 16-byte aligned or driver entry point missing)");
+    auto kernel = lora_down_kernel<kConvert>;
+    cudaError_t e = ensure_smem(kernel, kLdSmemBytes);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    const int m_tiles = (M + kLdRows - 1) / kLdRows;
+    const int num_kt = (K + kLdBK - 1) / kLdBK;
+    int ksplit = 1;
+    if (m_tiles < sm_count()) {
+        ksplit = sm_count() / m_tiles;
+        if (ksplit > 8) ksplit = 8;
+        if (ksplit > num_kt) ksplit = num_kt;
+        if (ksplit < 1) ksplit = 1;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(m_tiles) * static_cast<unsigned>(ksplit), 1, 1);
+    cfg.blockDim = dim3(kLdThreads, 1, 1);
+    cfg.dynamicSmemBytes = kLdSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(ksplit);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    e = cudaLaunchKernelEx(&cfg, kernel, tx, ta, static_cast<__half*>(t), M, K, R, ksplit);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    return static_cast<int>(cudaGetLastError());
+}
+
 }  // namespace convrot
 
 using namespace convrot;
@@ -1783,6 +1824,19 @@ CONVROT_API int ck_int4_convrot_gemm_a8(const void* X8, const void* Wp, const vo
     if (out_dtype == 1) return dispatch_gemm_a8<kOutBF16>(X8, Wp, xs, ws, b, out, M, N, K, lora, s);
     if (out_dtype == 0) return dispatch_gemm_a8<kOutF32>(X8, Wp, xs, ws, b, out, M, N, K, lora, s);
     return dispatch_gemm_a8<kOutS32>(X8, Wp, nullptr, nullptr, BiasRef{nullptr, 0}, out, M, N, K, lora, s);
+}
+
+CONVROT_API int ck_lora_down(const void* x, int in_dtype, const void* down, void* t, int M, int K, int R,
+                             void* stream) {
+    if (M < 0 || K <= 0 || K % 8 != 0) return fail("M must be >= 0 and K a positive multiple of 8");
+    if (R < 8 || R > 64 || R % 8 != 0) return fail("rank R must be a multiple of 8 in [8, 64]");
+    if (in_dtype != 1 && in_dtype != 2) return fail("in_dtype must be 1 (bf16) or 2 (f16)");
+    if (M == 0) return 0;
+    if (!x || !down || !t) return fail("null operand or output pointer");
+    if (!aligned16(x) || !aligned16(down) || !aligned16(t)) return fail("operands must be 16-byte aligned");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return in_dtype == 1 ? launch_lora_down<true>(x, down, t, M, K, R, s)
+                         : launch_lora_down<false>(x, down, t, M, K, R, s);
 }
 
 CONVROT_API int ck_int4_unpack(const void* packed, void* codes, long long rows, int K, void* stream) {

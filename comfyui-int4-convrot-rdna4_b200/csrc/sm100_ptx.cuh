@@ -473,3 +473,27 @@ __device__ __forceinline__ void tma_prefetch_l2_2d(const void* desc, int32_t x, 
 }
 
 }  // namespace convrot
+
+namespace convrot {
+
+// D[tmem] (+)= A[smem] * B[smem]^T on one SM, kind::f16 (A and B of one type,
+// fp16 or bf16 by the instruction descriptor), fp32 accumulator.
+__device__ __forceinline__ void mma_f16kind_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        :: "r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// 16-byte load from the shared memory of a CTA of this cluster (address from mapa_shared).
+__device__ __forceinline__ float4 ld_shared_cluster_f4(uint32_t cluster_addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(cluster_addr) : "memory");
+    return v;
+}
+
+}  // namespace convrot

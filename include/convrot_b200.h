@@ -172,6 +172,17 @@ int ck_int8_convrot_gemm(const void* X, const void* W, const void* xscale, const
  * parity checks, like ck_int4_gemm_s32). */
 int ck_int8_gemm_s32(const void* X, const void* W, void* acc, int M, int N, int K, void* stream);
 
+/* Dynamic-LoRA down projection T = fp16(x) . down^T (no HIP export counterpart;
+ * replaces the fp16 matmul the node's adapter runs on x, int4_ops.py:181-192,
+ * with the adapters in fp16 as int4_ops.py:165-167 prepares them):
+ *   x [M, K] in in_dtype (1 = bf16, converted to fp16 element by element with
+ *   round to nearest even, as a cast does; 2 = f16), down [R, K] f16,
+ *   t [M, R] f16 out; K % 8 == 0, R a multiple of 8 in [8, 64], all 16-byte
+ *   aligned. fp32 accumulation on the tensor cores, one rounding to fp16; the
+ *   summation order is fixed, so results repeat bit for bit. t is the lora_t
+ *   operand of the fused LoRA GEMMs. */
+int ck_lora_down(const void* x, int in_dtype, const void* down, void* t, int M, int K, int R, void* stream);
+
 /* The int4 GEMM on int8 activation codes (A8 form; no reference counterpart):
  *   X8 [M, K] int8, one sign-extended code per byte (ck_convrot_quant_int4_unpacked),
  *   Wp [N, K/2] packed int4 weights (the reference codec), both 16-byte aligned;

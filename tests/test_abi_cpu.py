@@ -183,3 +183,13 @@ def test_pick_groupsize_and_availability():
     assert _int4.pick_groupsize(40) is None
     if not torch.cuda.is_available():
         assert _int4.is_available() is False
+
+
+def test_lora_down_preconditions(lib):
+    f = lib.ck_lora_down
+    assert f(256, 1, 256, 256, 16, 260, 8, None) == -1 and b"K" in lib.ck_convrot_last_error()    # K % 8
+    assert f(256, 1, 256, 256, 16, 256, 12, None) == -1                                          # rank % 8
+    assert f(256, 1, 256, 256, 16, 256, 72, None) == -1                                          # rank > 64
+    assert f(256, 0, 256, 256, 16, 256, 8, None) == -1 and b"dtype" in lib.ck_convrot_last_error()
+    assert f(264, 1, 256, 256, 16, 256, 8, None) == -1 and b"aligned" in lib.ck_convrot_last_error()
+    assert f(256, 1, 256, 256, 0, 256, 8, None) == 0                                             # M = 0: no launch
