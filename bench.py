@@ -752,17 +752,33 @@ def nsplit_leg(device, rank, world, flush, stream, steps):
     if world == 1:
         return {"value": ops / (one_gpu * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": one_gpu,
                 "layer": "M=18432 12288->3072 +LoRA r=64, unsplit"}
+    from _int4.nsplit import PeerColumnSplit, convrot_w4a4_linear_peer_split, peer_split_supported
     q, w, b = shard_rows(down["qw"], down["ws"], down["bias"], rank, world)
     adapters = shard_adapters(down["adapters"], rank, world)
-    step = lambda: convrot_w4a4_linear_lora_nsplit(x, q, w, b, adapters, GROUP)
-    for _ in range(3):
-        out = step()
-    torch.cuda.synchronize()
-    ms = timed_steps(step, steps, flush, stream, world, device)
-    del out
+    gather = lambda: convrot_w4a4_linear_lora_nsplit(x, q, w, b, adapters, GROUP)
+    res = {}
+    split = PeerColumnSplit(device=device) if peer_split_supported(x, q.shape[0], GROUP) else None
+    legs = [("nccl_all_gather", gather)]
+    if split is not None:
+        legs.insert(0, ("peer_stores", lambda: convrot_w4a4_linear_peer_split(x, q, w, b, adapters, split, GROUP)))
+    for name, step in legs:
+        for _ in range(3):
+            out = step()
+        torch.cuda.synchronize()
+        res[name] = timed_steps(step, steps, flush, stream, world, device)
+        del out
+    if split is not None:
+        split.close()
+    name = "peer_stores" if split is not None else "nccl_all_gather"
+    ms = res[name]
     return {"value": ops / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms, "one_gpu_ms": one_gpu,
             "speedup_vs_one_gpu": one_gpu / ms if one_gpu else None,
-            "layer": f"M=18432 12288->3072 +LoRA r=64, N split x{world}, all-gather over NVLink"}
+            "exchange": ("each rank's GEMM writes its column block into its own [M, N] buffer in row chunks; "
+                         "copy engines carry each chunk to every peer over NVLink (CUDA IPC peer mappings) "
+                         "while the next chunk computes; bounded flag barrier" if split is not None
+                         else "NCCL all-gather, then a permute copy into [M, N]"),
+            "nccl_all_gather_ms": res["nccl_all_gather"],
+            "layer": f"M=18432 12288->3072 +LoRA r=64, N split x{world}"}
 
 
 # ---------------------------------------------------------------- the GPU arm

@@ -39,6 +39,13 @@ _SIGNATURES = {
     "ck_int8_convrot_gemm_lora": [_P] * 5 + [_I, _P] + [_I] * 4 + [_P, _P, _I, ctypes.c_float, _P],
     "ck_int4_unpack": [_P, _P, ctypes.c_longlong, _I, _P],
     "ck_lora_down": [_P, _I, _P, _P, _I, _I, _I, _P],
+    "ck_peer_buffer_alloc": [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), _P],
+    "ck_peer_buffer_open": [_P, ctypes.POINTER(ctypes.c_void_p)],
+    "ck_peer_buffer_close": [_P],
+    "ck_peer_buffer_free": [_P],
+    "ck_peer_barrier": [_P, _I, _I, _P, ctypes.c_longlong, _P],
+    "ck_peer_copy_columns": [_P, _I, _P] + [ctypes.c_longlong] * 4 + [_P],
+    "ck_int4_convrot_gemm_a8_peers": [_P] * 5 + [_I, _P] + [_I] * 7 + [_P, _P, _I, ctypes.c_float, _P],
     "ck_int4_convrot_gemm_a8": [_P] * 5 + [_I, _P] + [_I] * 4 + [_P, _P, _I, ctypes.c_float, _P],
     "ck_convrot_quant_int4_unpacked": [_P, _I, _P, _P, _I, _I, _I, _P],
     "ck_convrot_w4a4_linear_unpacked_workspace_size": [_I, _I],
@@ -449,6 +456,80 @@ def lora_down(x: torch.Tensor, down: torch.Tensor) -> torch.Tensor:
     rc = lib.ck_lora_down(x.data_ptr(), _IN_DTYPE_CODE[x.dtype], down.data_ptr(), t.data_ptr(), m, k, r, _stream(x))
     _check("ck_lora_down", rc)
     return t
+
+
+# --------------------------------------------------------------------- peer memory (column split)
+
+
+def peer_buffer_alloc(nbytes: int) -> tuple[int, bytes]:
+    """A zeroed device buffer of this process and its CUDA IPC handle (64 bytes)."""
+    lib = _load()
+    ptr = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(64)
+    _check("ck_peer_buffer_alloc", lib.ck_peer_buffer_alloc(nbytes, ctypes.byref(ptr), handle))
+    return int(ptr.value), bytes(handle.raw)
+
+
+def peer_buffer_open(handle: bytes) -> int:
+    """This process's mapping of another process's buffer (from peer_buffer_alloc's handle)."""
+    lib = _load()
+    ptr = ctypes.c_void_p()
+    _check("ck_peer_buffer_open", lib.ck_peer_buffer_open(ctypes.create_string_buffer(handle, 64), ctypes.byref(ptr)))
+    return int(ptr.value)
+
+
+def peer_buffer_close(ptr: int) -> None:
+    _check("ck_peer_buffer_close", _load().ck_peer_buffer_close(ptr))
+
+
+def peer_buffer_free(ptr: int) -> None:
+    _check("ck_peer_buffer_free", _load().ck_peer_buffer_free(ptr))
+
+
+def _ptr_array(ptrs):
+    return (ctypes.c_void_p * len(ptrs))(*ptrs)
+
+
+def peer_barrier(flag_ptrs, rank: int, counter_ptr: int, timeout_ns: int, device) -> None:
+    """Flag barrier after peer stores (ck_peer_barrier) on the device's current stream."""
+    lib = _load()
+    stream = torch.cuda.current_stream(device).cuda_stream
+    _check("ck_peer_barrier", lib.ck_peer_barrier(_ptr_array(flag_ptrs), len(flag_ptrs), rank, counter_ptr,
+                                                  int(timeout_ns), stream))
+
+
+def peer_copy_columns(dsts, src_ptr: int, pitch_bytes: int, offset_bytes: int, width_bytes: int, rows: int,
+                      stream) -> None:
+    """2D copies of a column block from src to every destination (ck_peer_copy_columns)."""
+    lib = _load()
+    _check("ck_peer_copy_columns", lib.ck_peer_copy_columns(_ptr_array(dsts), len(dsts), src_ptr, pitch_bytes,
+                                                            offset_bytes, width_bytes, rows, stream.cuda_stream))
+
+
+def int4_convrot_gemm_a8_peers(x_codes, w_packed, x_scale, w_scale, bias, out_dtype, outs, ldo: int, col0: int,
+                               lora_t=None, lora_b=None, lora_scale: float = 0.0) -> None:
+    """ck_int4_convrot_gemm_a8_peers: the A8 GEMM storing its [M, N] block at columns
+    col0 .. col0 + N of the [M, ldo] matrices at the device pointers ``outs``."""
+    lib = _load()
+    _require_cuda(x_codes, w_packed)
+    m, k = x_codes.shape
+    n, kp = w_packed.shape
+    if kp * 2 != k:
+        raise ValueError(f"K mismatch: codes {tuple(x_codes.shape)} w {tuple(w_packed.shape)}")
+    x_scale = x_scale.to(torch.float32).contiguous()
+    w_scale = w_scale.to(torch.float32).contiguous()
+    bias, bias_ptr, bias_code = _bias_arg(bias)
+    r = 0
+    if lora_t is not None:
+        lora_t = lora_t.to(torch.float16).contiguous()
+        lora_b = lora_b.to(torch.float16).contiguous()
+        r = lora_t.shape[1]
+    rc = lib.ck_int4_convrot_gemm_a8_peers(
+        x_codes.data_ptr(), w_packed.data_ptr(), x_scale.data_ptr(), w_scale.data_ptr(), bias_ptr, bias_code,
+        _ptr_array(outs), len(outs), ldo, col0, m, n, k, _OUT_DTYPE_CODE[out_dtype],
+        lora_t.data_ptr() if lora_t is not None else None, lora_b.data_ptr() if lora_b is not None else None,
+        r, float(lora_scale), _stream(x_codes))
+    _check("ck_int4_convrot_gemm_a8_peers", rc)
 
 
 # --------------------------------------------------------------------- unpacked-code path

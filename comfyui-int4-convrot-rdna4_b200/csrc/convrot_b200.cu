@@ -53,6 +53,7 @@ enum : int {
     kStatusTimeoutExpand = 3,
     kStatusTimeoutEpilogue = 4,
     kStatusTimeoutSelfTest = 5,
+    kStatusTimeoutPeer = 6,
 };
 
 __device__ __forceinline__ void record_status(int code) { atomicCAS(&g_device_status, 0, code); }
@@ -1147,7 +1148,8 @@ struct LoraArgs {
 
 template <int BN, bool SWAP, int OUT, bool STAGED, bool LORA, bool I8 = false, bool A8 = false>
 int launch_pair_impl(const void* Xp, const void* Wp, const float* xs, const float* ws, BiasRef bias,
-                     void* out, int M, int N, int K, const LoraArgs& lora, cudaStream_t stream) {
+                     void* out, int M, int N, int K, const LoraArgs& lora, cudaStream_t stream,
+                     const PeerOut& peers = PeerOut{}) {
     using Cfg = PairCfg<BN, STAGED, SWAP, LORA, I8, A8>;
     const void* a_ptr = SWAP ? Wp : Xp;
     const void* b_ptr = SWAP ? Xp : Wp;
@@ -1195,7 +1197,7 @@ int launch_pair_impl(const void* Xp, const void* Wp, const float* xs, const floa
     cfg.attrs = attr;
     cfg.numAttrs = 2;
     e = cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, tlt, tlb, xs, ws, bias, out, M, N, K, tiles_a,
-                           static_cast<int>(num_tiles), lora.scale, b_ptr);
+                           static_cast<int>(num_tiles), lora.scale, b_ptr, peers);
     if (e != cudaSuccess) return static_cast<int>(e);
     return static_cast<int>(cudaGetLastError());
 }
@@ -1940,4 +1942,166 @@ CONVROT_API int ck_convrot_device_status(void* stream, int* status) {
     e = cudaMemcpyToSymbolAsync(g_device_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     return static_cast<int>(e);
+}
+
+// ---------------------------------------------------------------------------
+// Column-split linear over peer memory (no reference counterpart: the
+// reference runs on one device). Each rank's GEMM stores its column block into
+// every rank's [M, ldo] output through peer mappings (CUDA IPC, plain stores
+// over NVLink, no multicast), then a flag barrier tells each rank that every
+// peer's block has landed in its own output.
+// ---------------------------------------------------------------------------
+
+namespace convrot {
+
+struct PeerFlags {
+    unsigned* ptr[8];       // rank p's flag words (this process's mapping); slot q = written by rank q
+};
+
+// One warp: thread p signals rank p (slot `rank` of its flags) with this call's
+// epoch, then waits, bounded, for rank p's signal in its own slot p. The epoch
+// is a per-process device counter, so the kernel can be replayed from a graph.
+__global__ void peer_barrier_kernel(PeerFlags f, int nranks, int rank, unsigned* counter,
+                                    unsigned long long limit_ns) {
+    const int p = threadIdx.x;
+    unsigned epoch = 0u;
+    if (p == 0) {
+        epoch = *counter + 1u;
+        *counter = epoch;
+    }
+    epoch = __shfl_sync(0xFFFFFFFFu, epoch, 0);
+    if (p >= nranks) return;
+    __threadfence_system();                           // the stores of the kernels before this one
+    asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(f.ptr[p] + rank), "r"(epoch) : "memory");
+    const unsigned* mine = f.ptr[rank] + p;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+        if (static_cast<int>(v - epoch) >= 0) break;
+        if (globaltimer_ns() - t0 > limit_ns) {
+            record_status(kStatusTimeoutPeer);
+            break;
+        }
+        __nanosleep(64);
+    }
+}
+
+}  // namespace convrot
+
+CONVROT_API int ck_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+    if (!ptr || !ipc_handle || bytes == 0) return fail("null pointer or zero size");
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    e = cudaMemset(p, 0, bytes);
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return static_cast<int>(e);
+    }
+    *ptr = p;
+    return 0;
+}
+
+CONVROT_API int ck_peer_buffer_open(const void* ipc_handle, void** ptr) {
+    if (!ptr || !ipc_handle) return fail("null pointer");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof(h));
+    return static_cast<int>(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+CONVROT_API int ck_peer_buffer_close(void* ptr) {
+    return ptr ? static_cast<int>(cudaIpcCloseMemHandle(ptr)) : 0;
+}
+
+CONVROT_API int ck_peer_buffer_free(void* ptr) {
+    return ptr ? static_cast<int>(cudaFree(ptr)) : 0;
+}
+
+CONVROT_API int ck_peer_barrier(void* const* flags, int nranks, int rank, void* counter, long long timeout_ns,
+                                void* stream) {
+    if (nranks < 1 || nranks > 8 || rank < 0 || rank >= nranks) return fail("nranks in [1, 8], 0 <= rank < nranks");
+    if (!flags || !counter) return fail("null flag or counter pointer");
+    if (timeout_ns <= 0 || timeout_ns > 60000000000LL) return fail("timeout_ns must be in (0, 6e10]");
+    PeerFlags f{};
+    for (int p = 0; p < nranks; ++p) {
+        if (!flags[p] || (reinterpret_cast<uintptr_t>(flags[p]) & 3u)) return fail("flag pointers must be 4-byte aligned");
+        f.ptr[p] = static_cast<unsigned*>(flags[p]);
+    }
+    peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+        f, nranks, rank, static_cast<unsigned*>(counter), static_cast<unsigned long long>(timeout_ns));
+    return static_cast<int>(cudaGetLastError());
+}
+
+CONVROT_API int ck_int4_convrot_gemm_a8_peers(const void* X8, const void* Wp, const void* xscale, const void* wscale,
+                                              const void* bias, int bias_dtype, void* const* outs, int nouts,
+                                              int ldo, int col0, int M, int N, int K, int out_dtype,
+                                              const void* lora_t, const void* lora_b, int rank,
+                                              float lora_scale, void* stream) {
+    if (M < 0 || N < 0 || K <= 0 || K % 128 != 0 || K > 65536)
+        return fail("M, N must be >= 0 and K a multiple of 128 in [128, 65536]");
+    if (out_dtype != 0 && out_dtype != 1) return fail("out_dtype must be 0 (f32) or 1 (bf16)");
+    if (bias_dtype < 0 || bias_dtype > 2) return fail("bias_dtype must be 0 (f32), 1 (bf16) or 2 (f16)");
+    if (nouts < 1 || nouts > 8 || !outs) return fail("1 to 8 output pointers");
+    if (col0 < 0 || ldo < col0 + N || ldo % 8 != 0 || col0 % 8 != 0)
+        return fail("need 0 <= col0, col0 + N <= ldo, ldo and col0 multiples of 8");
+    const bool with_lora = lora_t != nullptr || lora_b != nullptr;
+    if (with_lora && (rank < 8 || rank > 64 || rank % 8 != 0)) return fail("LoRA rank must be a multiple of 8 in [8, 64]");
+    if (M == 0 || N == 0) return 0;
+    if (!X8 || !Wp || !xscale || !wscale) return fail("null operand or scale pointer");
+    if (!aligned16(X8) || !aligned16(Wp)) return fail("operands must be 16-byte aligned");
+    if (with_lora && (!lora_t || !lora_b || !aligned16(lora_t) || !aligned16(lora_b)))
+        return fail("LoRA operands must be non-null and 16-byte aligned");
+    PeerOut peers{};
+    for (int d = 0; d < nouts; ++d) {
+        if (!outs[d] || !aligned16(outs[d])) return fail("output pointers must be non-null and 16-byte aligned");
+        peers.ptr[d] = outs[d];
+    }
+    peers.count = nouts;
+    peers.ldo = ldo;
+    peers.col0 = col0;
+    LoraArgs lora;
+    if (with_lora) {
+        lora.t = lora_t;
+        lora.b = lora_b;
+        lora.rank = rank;
+        lora.scale = lora_scale;
+    }
+    const float* xs = static_cast<const float*>(xscale);
+    const float* ws = static_cast<const float*>(wscale);
+    const BiasRef b{bias, bias_dtype};
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // the direct-store A8 pair kernel: 256 x 256 tiles when they fill the CTA pairs
+    const bool wide = 2L * ((M + 255) / 256) * ((N + 255) / 256) >= sm_count();
+    if (out_dtype == 1) {
+        if (with_lora)
+            return wide ? launch_pair_impl<256, false, kOutBF16, false, true, false, true>(X8, Wp, xs, ws, b, nullptr, M, N, K, lora, s, peers)
+                        : launch_pair_impl<128, false, kOutBF16, false, true, false, true>(X8, Wp, xs, ws, b, nullptr, M, N, K, lora, s, peers);
+        return wide ? launch_pair_impl<256, false, kOutBF16, false, false, false, true>(X8, Wp, xs, ws, b, nullptr, M, N, K, lora, s, peers)
+                    : launch_pair_impl<128, false, kOutBF16, false, false, false, true>(X8, Wp, xs, ws, b, nullptr, M, N, K, lora, s, peers);
+    }
+    if (with_lora)
+        return wide ? launch_pair_impl<256, false, kOutF32, false, true, false, true>(X8, Wp, xs, ws, b, nullptr, M, N, K, lora, s, peers)
+                    : launch_pair_impl<128, false, kOutF32, false, true, false, true>(X8, Wp, xs, ws, b, nullptr, M, N, K, lora, s, peers);
+    return wide ? launch_pair_impl<256, false, kOutF32, false, false, false, true>(X8, Wp, xs, ws, b, nullptr, M, N, K, lora, s, peers)
+                : launch_pair_impl<128, false, kOutF32, false, false, false, true>(X8, Wp, xs, ws, b, nullptr, M, N, K, lora, s, peers);
+}
+
+CONVROT_API int ck_peer_copy_columns(void* const* dsts, int ndst, const void* src, long long pitch_bytes,
+                                     long long offset_bytes, long long width_bytes, long long rows, void* stream) {
+    if (ndst < 0 || ndst > 8 || (ndst > 0 && !dsts) || !src) return fail("0 to 8 destinations and a source");
+    if (pitch_bytes <= 0 || width_bytes <= 0 || offset_bytes < 0 || offset_bytes + width_bytes > pitch_bytes || rows < 0)
+        return fail("need 0 <= offset, offset + width <= pitch, rows >= 0");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const unsigned char* from = static_cast<const unsigned char*>(src) + offset_bytes;
+    for (int d = 0; d < ndst; ++d) {
+        if (!dsts[d]) return fail("null destination");
+        cudaError_t e = cudaMemcpy2DAsync(static_cast<unsigned char*>(dsts[d]) + offset_bytes,
+                                          static_cast<size_t>(pitch_bytes), from, static_cast<size_t>(pitch_bytes),
+                                          static_cast<size_t>(width_bytes), static_cast<size_t>(rows),
+                                          cudaMemcpyDefault, s);
+        if (e != cudaSuccess) return static_cast<int>(e);
+    }
+    return 0;
 }

@@ -221,7 +221,8 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                       const __grid_constant__ CUtensorMap tmap_lt, const __grid_constant__ CUtensorMap tmap_lb,
                       const float* __restrict__ xscale, const float* __restrict__ wscale,
                       BiasRef bias, void* __restrict__ out, int M, int N, int K,
-                      int tiles_a, int num_tiles, float lora_scale, const void* __restrict__ wraw) {
+                      int tiles_a, int num_tiles, float lora_scale, const void* __restrict__ wraw,
+                      const __grid_constant__ PeerOut peers) {
     using Cfg = PairCfg<BN, STAGED, SWAP, LORA, I8, A8>;
     static_assert(!LORA || !SWAP, "the LoRA side path is fused into non-swapped tiles");
     static_assert(!STAGED || (OUT == kOutBF16 && !SWAP), "staged epilogue is for bf16, non-swapped tiles");
@@ -812,7 +813,14 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
                             }
                         } else {
                             if (!lane_ok) continue;
-                            store_row32<OUT>(out, static_cast<size_t>(a) * N + b, b, N, v, vbias);
+                            if (peers.count == 0) {
+                                store_row32<OUT>(out, static_cast<size_t>(a) * N + b, b, N, v, vbias);
+                            } else {
+                                // column block of a wider [M, ldo] output on every rank
+                                const size_t o = static_cast<size_t>(a) * peers.ldo + peers.col0 + b;
+                                #pragma unroll 1
+                                for (int d = 0; d < peers.count; ++d) store_row32<OUT>(peers.ptr[d], o, b, N, v, vbias);
+                            }
                         }
                     }
                 }

@@ -23,6 +23,17 @@ struct BiasRef {
     }
 };
 
+// Extra output destinations of the pair GEMM's direct-store epilogue (the
+// column-split linear): every output row chunk goes to ptr[0 .. count) at
+// row * ldo + col0 + column instead of to `out` at row * N + column. Pointers
+// may be other GPUs' memory (peer mappings); count == 0: the plain output.
+struct PeerOut {
+    void* ptr[8];
+    int count;
+    int ldo;
+    int col0;
+};
+
 // Records `msg` for ck_convrot_last_error() and returns -1.
 int fail(const char* msg);
 

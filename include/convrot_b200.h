@@ -172,6 +172,50 @@ int ck_int8_convrot_gemm(const void* X, const void* W, const void* xscale, const
  * parity checks, like ck_int4_gemm_s32). */
 int ck_int8_gemm_s32(const void* X, const void* W, void* acc, int M, int N, int K, void* stream);
 
+/* Column-split linear over peer memory (no reference counterpart: the
+ * reference runs on one device). P ranks (one process per GPU) each own N/P
+ * weight rows; every rank's GEMM stores its column block straight into every
+ * rank's [M, ldo] output through peer mappings over NVLink, then
+ * ck_peer_barrier tells each rank that all blocks have landed in its output.
+ *
+ * ck_peer_buffer_alloc: cudaMalloc of `bytes` (zeroed) and its 64-byte CUDA IPC
+ * handle; ck_peer_buffer_open maps another process's buffer from its handle
+ * (ck_peer_buffer_close unmaps it); ck_peer_buffer_free frees an own buffer. */
+int ck_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+int ck_peer_buffer_open(const void* ipc_handle, void** ptr);
+int ck_peer_buffer_close(void* ptr);
+int ck_peer_buffer_free(void* ptr);
+
+/* ck_int4_convrot_gemm_a8 (packed weights, int8 activation codes, optional
+ * LoRA side path; same D, epilogue and output bits) storing its [M, N] result
+ * as columns col0 .. col0 + N of the [M, ldo] row-major matrices outs[0 ..
+ * nouts) (1 to 8 pointers, any of them peer mappings; ldo and col0 multiples
+ * of 8). Plain stores, no multicast. */
+int ck_int4_convrot_gemm_a8_peers(const void* X8, const void* Wp, const void* xscale, const void* wscale,
+                                  const void* bias, int bias_dtype, void* const* outs, int nouts,
+                                  int ldo, int col0, int M, int N, int K, int out_dtype,
+                                  const void* lora_t, const void* lora_b, int rank,
+                                  float lora_scale, void* stream);
+
+/* Barrier of nranks (<= 8) ranks after their peer stores: flags[p] is rank p's
+ * flag array (int32 [nranks], this process's mapping of it; zero when
+ * allocated), counter a 4-byte device word of this rank (zero at the start,
+ * advanced by every call, so the call can sit in a CUDA graph). Rank `rank`
+ * writes this call's epoch into slot `rank` of every rank's flags (release,
+ * system scope, after a system fence) and waits until every slot of its own
+ * flags has reached it. A wait longer than timeout_ns records status 6
+ * (ck_convrot_device_status) and returns instead of hanging. Every rank must
+ * make the same sequence of calls. */
+int ck_peer_barrier(void* const* flags, int nranks, int rank, void* counter, long long timeout_ns, void* stream);
+
+/* Copy columns [offset, offset + width) (bytes) of `rows` rows of pitch
+ * pitch_bytes from src to the same place in each of dsts[0 .. ndst) (peer
+ * mappings allowed): one 2D copy per destination on `stream`, carried by the
+ * copy engines over NVLink, so no SM time is taken from kernels running beside
+ * it. The column-split linear sends each rank's block to its peers this way. */
+int ck_peer_copy_columns(void* const* dsts, int ndst, const void* src, long long pitch_bytes,
+                         long long offset_bytes, long long width_bytes, long long rows, void* stream);
+
 /* Dynamic-LoRA down projection T = fp16(x) . down^T (no HIP export counterpart;
  * replaces the fp16 matmul the node's adapter runs on x, int4_ops.py:181-192,
  * with the adapters in fp16 as int4_ops.py:165-167 prepares them):
