@@ -145,6 +145,38 @@ def convrot_w4a4_linear(
     return out.reshape(*shape[:-1], qweight.shape[0])
 
 
+def convrot_w4a4_linear_lnmod(
+    x: torch.Tensor,
+    qweight: torch.Tensor,
+    wscales: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    shift: torch.Tensor | None = None,
+    scale: torch.Tensor | None = None,
+    eps: float = 1e-6,
+    convrot_groupsize: int = 256,
+) -> torch.Tensor:
+    """``convrot_w4a4_linear((1 + scale) * LayerNorm(x) + shift, ...)`` in one pass over x.
+
+    The rotation moved into the producer of x: a Flux block's QKV and MLP-up
+    projections take ``(1 + mod.scale) * norm(x) + mod.shift`` (LayerNorm
+    without affine, eps 1e-6), and here the normalisation and modulation run in
+    the kernel that rotates and quantizes the rows, so the normalised bf16
+    tensor never goes to memory. x bf16 [..., K] (K % 256 == 0, K <= 6144), shift /
+    scale bf16 [K] (one vector for all rows; None = zeros). The statistics use a
+    fixed fp32 order (``ck_convrot_quant_int4_lnmod``), within rounding of
+    torch's LayerNorm. Returns [..., N] in bf16.
+    """
+    _validate(x, qweight, convrot_groupsize, _INT4_GROUP_SIZE, "int4")
+    if not cuda_loader.lnmod_supported(x, convrot_groupsize):
+        raise ValueError("the fused LayerNorm linear takes bf16 CUDA rows of whole 256-column tiles "
+                         "(K <= 6144, convrot_groupsize 64 or 256)")
+    shape = x.shape
+    x2d = x.reshape(-1, shape[-1]).contiguous()
+    out = cuda_loader.convrot_w4a4_linear_lnmod(x2d, qweight, wscales, bias, scale, shift, eps, torch.bfloat16,
+                                                convrot_groupsize)
+    return out.reshape(*shape[:-1], qweight.shape[0])
+
+
 _MAX_LORA_RANK = 64
 # Unit roundoff of the side path's operand type (T = x.A^T and B enter the
 # tensor cores in fp16, the reference's adapter dtype, int4_ops.py:165-167): the

@@ -39,6 +39,9 @@ _SIGNATURES = {
     "ck_int8_convrot_gemm_lora": [_P] * 5 + [_I, _P] + [_I] * 4 + [_P, _P, _I, ctypes.c_float, _P],
     "ck_int4_unpack": [_P, _P, ctypes.c_longlong, _I, _P],
     "ck_lora_down": [_P, _I, _P, _P, _I, _I, _I, _P],
+    "ck_convrot_quant_int4_lnmod": [_P, _P, _P, ctypes.c_float, _P, _P, _I, _I, _I, _I, _P],
+    "ck_convrot_w4a4_linear_lnmod": [_P, _P, _P, ctypes.c_float, _P, _P, _P, _I, _P] + [_I] * 5
+                                    + [_P, ctypes.c_size_t, _P],
     "ck_peer_buffer_alloc": [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), _P],
     "ck_peer_buffer_open": [_P, ctypes.POINTER(ctypes.c_void_p)],
     "ck_peer_buffer_close": [_P],
@@ -434,6 +437,72 @@ def int8_gemm_s32(x_int8, w_int8):
     rc = lib.ck_int8_gemm_s32(x_int8.data_ptr(), w_int8.data_ptr(), acc.data_ptr(), m, n, k, _stream(x_int8))
     _check("ck_int8_gemm_s32", rc)
     return acc
+
+
+# --------------------------------------------------------------------- LayerNorm + modulation fused
+
+
+def _mod_vector(v, k: int, device):
+    if v is None:
+        return None, None
+    v = v.reshape(-1).to(device=device, dtype=torch.bfloat16).contiguous()
+    if v.numel() != k:
+        raise ValueError(f"modulation vector of {v.numel()} values for K={k}")
+    return v, v.data_ptr()
+
+
+def convrot_quant_int4_lnmod(x, scale, shift, eps: float, convrot_groupsize: int, unpacked: bool = False):
+    """Codes and scales of bf16((1 + scale) * LayerNorm(x) + shift), rotated and quantized in
+    one pass over x (ck_convrot_quant_int4_lnmod): packed [M, K/2] or one int8 per code [M, K]."""
+    lib = _load()
+    _require_cuda(x)
+    if x.dtype != torch.bfloat16:
+        raise ValueError("the fused LayerNorm quantizer takes bf16 activations")
+    x = x.contiguous()
+    m, k = x.shape
+    sc, sc_ptr = _mod_vector(scale, k, x.device)
+    sh, sh_ptr = _mod_vector(shift, k, x.device)
+    q = torch.empty((m, k if unpacked else k // 2), dtype=torch.int8, device=x.device)
+    s = torch.empty((m,), dtype=torch.float32, device=x.device)
+    rc = lib.ck_convrot_quant_int4_lnmod(x.data_ptr(), sc_ptr, sh_ptr, float(eps), q.data_ptr(), s.data_ptr(), m, k,
+                                         convrot_groupsize, 1 if unpacked else 0, _stream(x))
+    _check("ck_convrot_quant_int4_lnmod", rc)
+    return q, s
+
+
+def convrot_w4a4_linear_lnmod(x, w_packed, w_scale, bias, scale, shift, eps: float, out_dtype,
+                              convrot_groupsize: int = 256):
+    """The int4 linear of bf16((1 + scale) * LayerNorm(x) + shift) (ck_convrot_w4a4_linear_lnmod)."""
+    lib = _load()
+    _require_cuda(x, w_packed)
+    if x.dtype != torch.bfloat16:
+        raise ValueError("the fused LayerNorm linear takes bf16 activations")
+    x = x.contiguous()
+    w_packed = w_packed.contiguous()
+    m, k = x.shape
+    n, kp = w_packed.shape
+    if kp * 2 != k:
+        raise ValueError(f"K mismatch: x {tuple(x.shape)} w {tuple(w_packed.shape)}")
+    sc, sc_ptr = _mod_vector(scale, k, x.device)
+    sh, sh_ptr = _mod_vector(shift, k, x.device)
+    w_scale = w_scale.to(torch.float32).contiguous()
+    bias, bias_ptr, bias_code = _bias_arg(bias)
+    out = torch.empty((m, n), dtype=out_dtype, device=x.device)
+    ws_bytes = lib.ck_convrot_w4a4_linear_workspace_size(m, k)
+    workspace = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=x.device)
+    rc = lib.ck_convrot_w4a4_linear_lnmod(x.data_ptr(), sc_ptr, sh_ptr, float(eps), w_packed.data_ptr(),
+                                          w_scale.data_ptr(), bias_ptr, bias_code, out.data_ptr(),
+                                          _OUT_DTYPE_CODE[out_dtype], m, n, k, convrot_groupsize,
+                                          workspace.data_ptr(), ws_bytes, _stream(x))
+    _check("ck_convrot_w4a4_linear_lnmod", rc)
+    return out
+
+
+def lnmod_supported(x: torch.Tensor, convrot_groupsize: int) -> bool:
+    """bf16 CUDA rows of whole 256-column tiles, K <= 6144, G in {64, 256}."""
+    k = x.shape[-1]
+    return (x.is_cuda and x.dtype == torch.bfloat16 and convrot_groupsize in (64, 256) and k % 256 == 0
+            and k <= 6144)
 
 
 # --------------------------------------------------------------------- Dynamic-LoRA down projection

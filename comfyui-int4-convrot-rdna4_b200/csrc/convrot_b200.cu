@@ -526,10 +526,80 @@ __device__ __forceinline__ uint32_t bf16x2_add(uint32_t a, uint32_t b) {
 #ifndef CONVROT_Q5_MIN_BLOCKS
 #define CONVROT_Q5_MIN_BLOCKS 1
 #endif
-template <int G, int BITS, bool UNPACKED = false>
+// LNMOD: the rows are first normalised and modulated as the producer of x
+// before a Flux block's QKV or MLP-up projection does,
+//   y = bf16(bf16(bf16(1 + scale[k]) * xn) + shift[k]),  xn = bf16((x - mean) * rstd),
+// LayerNorm without affine over the row (biased variance, eps), all in fp32 in a
+// fixed order: lane l of a warp sums elements l, l + 32, ... of the row (from
+// the slab in shared memory), then an xor butterfly over the 32 lane sums;
+// mean = sum / K; the squared deviations (x - mean)^2 (two roundings) likewise;
+// rstd = 1 / sqrt(var + eps), each step rounded. y then goes through the
+// rotation and the quantizer as x would; the normalised tensor never touches HBM.
+struct LnModArgs {
+    const __nv_bfloat16* scale;     // [K] or nullptr (scale 0)
+    const __nv_bfloat16* shift;     // [K] or nullptr (shift 0)
+    float eps;
+};
+constexpr int kQ5LnMaxK = 6144;     // the staged modulation vectors share the block's shared memory
+// extra shared memory of the LNMOD form: row statistics [rows][mean, rstd] and
+// the staged bf16(1 + scale) and shift vectors
+constexpr int q5_lnmod_bytes(int K) { return kQ5MaxTiles * 16 + 4 * K; }
+
+// p[0] + p[1] + ... + p[n-1] left to right (n >= 1); the loads of eight
+// partials are issued before their additions.
+__device__ __forceinline__ float q5_ordered_sum(const float* p, int n) {
+    float acc = p[0];
+    int i = 1;
+    for (; i + 8 <= n; i += 8) {
+        float v[8];
+        #pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = p[i + j];
+        #pragma unroll
+        for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, v[j]);
+    }
+    for (; i < n; ++i) acc = __fadd_rn(acc, p[i]);
+    return acc;
+}
+
+// Sum of a thread's 128 bf16 values in the slab (its 16 chunks of 8, read in
+// slot order, chunk s ^ kx in slot s) -- or, with sq, of (v - mean)^2 (two
+// roundings each): a binary tree over the 8 values of each chunk, then over
+// slots 0..7 and 8..15 apart, then their sum. Under the XOR relabelling the
+// aligned pairs, quads and octets of slots are those of the chunks, so the
+// value is the one of the same tree in memory order.
+__device__ __forceinline__ float q5_slab_tree_sum(const unsigned char* src, int kx, bool sq, float mean) {
+    float c[16];
+    #pragma unroll
+    for (int s = 0; s < 16; ++s) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(src + 16 * (s ^ kx));
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+        float v[8];
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            v[2 * i] = __uint_as_float(w[i] << 16);
+            v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+        }
+        if (sq) {
+            #pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float d = __fsub_rn(v[e], mean);
+                v[e] = __fmul_rn(d, d);
+            }
+        }
+        c[s] = __fadd_rn(__fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3])),
+                         __fadd_rn(__fadd_rn(v[4], v[5]), __fadd_rn(v[6], v[7])));
+    }
+    #pragma unroll
+    for (int w = 8; w > 0; w >>= 1)
+        #pragma unroll
+        for (int s = 0; s < w; ++s) c[s] = __fadd_rn(c[2 * s], c[2 * s + 1]);
+    return c[0];
+}
+
+template <int G, int BITS, bool UNPACKED = false, bool LNMOD = false>
 __global__ void __launch_bounds__(kQ5MaxThreads, CONVROT_Q5_MIN_BLOCKS)
 convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restrict__ qout,
-                          float* __restrict__ scaleout, int M, int K, int rows_per_round) {
+                          float* __restrict__ scaleout, int M, int K, int rows_per_round, LnModArgs lnmod) {
     static_assert(G == 64 || G == 256, "two-digit tiles only");
     static_assert(BITS == 4 || BITS == 8, "int4 or int8 codes");
     static_assert(!UNPACKED || BITS == 4, "int8 codes are never packed");
@@ -569,6 +639,48 @@ convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restric
         if (blockIdx.x < rounds) issue(blockIdx.x, 0);
         if (blockIdx.x + gridDim.x < rounds) issue(blockIdx.x + gridDim.x, 1);
     }
+    // LNMOD shared memory after the two slabs: the threads' partial sums (two
+    // arrays: sums, squared deviations), bf16(1 + scale)[K], shift[K]
+    float* ln_part = reinterpret_cast<float*>(slab + 2 * slab_bytes);
+    float* ln_part2 = ln_part + 2 * kQ5MaxTiles;
+    __nv_bfloat16* ln_s1 = reinterpret_cast<__nv_bfloat16*>(ln_part2 + 2 * kQ5MaxTiles);
+    __nv_bfloat16* ln_sh = ln_s1 + K;
+    if constexpr (LNMOD) {
+        // eight columns per step, all loads of a thread issued before their use
+        const bool vec = !(reinterpret_cast<uintptr_t>(lnmod.scale) & 15u) && !(reinterpret_cast<uintptr_t>(lnmod.shift) & 15u);
+        #pragma unroll 4
+        for (int c = tid; c < K / 8; c += blockDim.x) {
+            uint32_t sw[4] = {0u, 0u, 0u, 0u}, hw[4] = {0u, 0u, 0u, 0u};
+            if (vec) {
+                if (lnmod.scale != nullptr) {
+                    const uint4 v = __ldg(reinterpret_cast<const uint4*>(lnmod.scale) + c);
+                    sw[0] = v.x; sw[1] = v.y; sw[2] = v.z; sw[3] = v.w;
+                }
+                if (lnmod.shift != nullptr) {
+                    const uint4 v = __ldg(reinterpret_cast<const uint4*>(lnmod.shift) + c);
+                    hw[0] = v.x; hw[1] = v.y; hw[2] = v.z; hw[3] = v.w;
+                }
+            } else {
+                #pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t lo_s = lnmod.scale ? __bfloat16_as_ushort(lnmod.scale[8 * c + 2 * i]) : 0u;
+                    const uint32_t hi_s = lnmod.scale ? __bfloat16_as_ushort(lnmod.scale[8 * c + 2 * i + 1]) : 0u;
+                    const uint32_t lo_h = lnmod.shift ? __bfloat16_as_ushort(lnmod.shift[8 * c + 2 * i]) : 0u;
+                    const uint32_t hi_h = lnmod.shift ? __bfloat16_as_ushort(lnmod.shift[8 * c + 2 * i + 1]) : 0u;
+                    sw[i] = lo_s | (hi_s << 16);
+                    hw[i] = lo_h | (hi_h << 16);
+                }
+            }
+            uint32_t s1[4];
+            #pragma unroll
+            for (int i = 0; i < 4; ++i)
+                s1[i] = bf16x2_bits(__fadd_rn(1.0f, __uint_as_float(sw[i] << 16)),
+                                    __fadd_rn(1.0f, __uint_as_float(sw[i] & 0xFFFF0000u)));
+            reinterpret_cast<uint4*>(ln_s1)[c] = make_uint4(s1[0], s1[1], s1[2], s1[3]);
+            reinterpret_cast<uint4*>(ln_sh)[c] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        }
+        __syncthreads();
+    }
 
     int it = 0;
     for (int rd = blockIdx.x; rd < rounds; rd += gridDim.x, ++it) {
@@ -584,13 +696,57 @@ convrot_quant_bf16_kernel(const __nv_bfloat16* __restrict__ x, int8_t* __restric
         uint32_t packed[8][8];                         // rounded rotated values, bf16 pairs
         // a tile's two halves are lanes l and l ^ 16: both in or both out
         const unsigned mask = __ballot_sync(0xFFFFFFFFu, active && ok);
+        float ln_mean = 0.0f, ln_rstd = 0.0f;
+        if constexpr (LNMOD) {
+            // row statistics: every thread reduces its own 128 values of the slab
+            // (binary trees over the 8 values of a chunk and over the 16 chunks,
+            // read in the lane's XOR order: a tree over aligned pairs, quads, ...
+            // has the same value in either order, the sums only commute), then adds
+            // its row's 2 K / 256 partials in order; the variance likewise
+            const bool live = active && ok;
+            const unsigned char* lsrc = slab + buf * slab_bytes + tile * 512 + h * 256;
+            const int seg = 2 * tile + h;
+            const int seg0 = 2 * (my_row * ntile);
+            const int nseg = 2 * ntile;
+            ln_part[seg] = live ? q5_slab_tree_sum(lsrc, kx, false, 0.0f) : 0.0f;
+            __syncthreads();
+            if (live) ln_mean = __fdiv_rn(q5_ordered_sum(ln_part + seg0, nseg), static_cast<float>(K));
+            ln_part2[seg] = live ? q5_slab_tree_sum(lsrc, kx, true, ln_mean) : 0.0f;
+            __syncthreads();
+            if (live) {
+                const float var = __fdiv_rn(q5_ordered_sum(ln_part2 + seg0, nseg), static_cast<float>(K));
+                ln_rstd = __frcp_rn(__fsqrt_rn(__fadd_rn(var, lnmod.eps)));
+            }
+        }
+        float2 V[8][8];
         if (active && ok) {
             const unsigned char* src = slab + buf * slab_bytes + tile * 512 + h * 256;
-            float2 V[8][8];
             #pragma unroll
             for (int s = 0; s < 16; ++s) {
                 const uint4 raw = *reinterpret_cast<const uint4*>(src + 16 * (s ^ kx));
-                const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+                uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+                if constexpr (LNMOD) {
+                    // y = bf16(bf16(bf16(1 + scale) * bf16((x - mean) * rstd)) + shift);
+                    // columns tile_in_row * 256 + h * 128 + 8 (s ^ kx) + 0..7
+                    const int col = tile_in_row * 256 + h * 128 + 8 * (s ^ kx);
+                    const uint4 s1v = *reinterpret_cast<const uint4*>(ln_s1 + col);
+                    const uint4 shv = *reinterpret_cast<const uint4*>(ln_sh + col);
+                    const uint32_t s1w[4] = {s1v.x, s1v.y, s1v.z, s1v.w};
+                    const uint32_t shw[4] = {shv.x, shv.y, shv.z, shv.w};
+                    // paired fp32 (x - mean = x + (-mean) exactly); every product goes
+                    // through a bf16 rounding before any sum, so nothing can contract
+                    const float2 nm = make_float2(-ln_mean, -ln_mean), rs = make_float2(ln_rstd, ln_rstd);
+                    auto unpack = [](uint32_t b) {
+                        return make_float2(__uint_as_float(b << 16), __uint_as_float(b & 0xFFFF0000u));
+                    };
+                    #pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 xn = fmul2_rn(fadd2_rn(unpack(w[i]), nm), rs);
+                        const float2 t2 = fmul2_rn(unpack(s1w[i]), unpack(bf16x2_bits(xn.x, xn.y)));
+                        const float2 y = fadd2_rn(unpack(bf16x2_bits(t2.x, t2.y)), unpack(shw[i]));
+                        w[i] = bf16x2_bits(y.x, y.y);
+                    }
+                }
                 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const float lo = __uint_as_float(w[i] << 16), hi = __uint_as_float(w[i] & 0xFFFF0000u);
@@ -1450,8 +1606,9 @@ int launch_quant_t(const void* x, void* q, void* s, int M, int K, cudaStream_t s
 }
 
 // bf16 rows of whole 256-column tiles, G in {64, 256}: the two-threads-per-tile kernel.
-template <int G, int BITS, bool UNPACKED = false>
-int launch_quant_bf16_tiles(const void* x, void* q, void* s, int M, int K, cudaStream_t stream) {
+template <int G, int BITS, bool UNPACKED = false, bool LNMOD = false>
+int launch_quant_bf16_tiles(const void* x, void* q, void* s, int M, int K, cudaStream_t stream,
+                            LnModArgs lnmod = LnModArgs{nullptr, nullptr, 0.0f}) {
     const int ntile = K / 256;
     // Rounds of about kQ5RoundTiles tiles let several blocks share an SM (their
     // phases drift apart, which mixes the FMA-heavy rotation with the ALU-heavy
@@ -1465,9 +1622,9 @@ int launch_quant_bf16_tiles(const void* x, void* q, void* s, int M, int K, cudaS
     if (rows > per_block) rows = per_block;            // small M: spread the rows over the SMs
     if (rows < 1) rows = 1;
     const int tiles = (rows * ntile + 15) / 16 * 16;
-    const int smem = q5_smem_bytes(2 * tiles);
-    auto kernel = convrot_quant_bf16_kernel<G, BITS, UNPACKED>;
-    cudaError_t e = ensure_smem(kernel, q5_smem_bytes(kQ5MaxThreads));
+    const int smem = q5_smem_bytes(2 * tiles) + (LNMOD ? q5_lnmod_bytes(K) : 0);
+    auto kernel = convrot_quant_bf16_kernel<G, BITS, UNPACKED, LNMOD>;
+    cudaError_t e = ensure_smem(kernel, q5_smem_bytes(kQ5MaxThreads) + (LNMOD ? q5_lnmod_bytes(kQ5LnMaxK) : 0));
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  static_cast<int>(cudaSharedmemCarveoutMaxShared));
@@ -1475,7 +1632,8 @@ int launch_quant_bf16_tiles(const void* x, void* q, void* s, int M, int K, cudaS
     const int rounds = (M + rows - 1) / rows;
     const int grid = rounds < slots ? rounds : slots;
     e = launch_pdl(kernel, dim3(grid), dim3(2 * tiles), static_cast<size_t>(smem), stream,
-                   static_cast<const __nv_bfloat16*>(x), static_cast<int8_t*>(q), static_cast<float*>(s), M, K, rows);
+                   static_cast<const __nv_bfloat16*>(x), static_cast<int8_t*>(q), static_cast<float*>(s), M, K, rows,
+                   lnmod);
     return static_cast<int>(e);
 }
 
@@ -2104,4 +2262,70 @@ CONVROT_API int ck_peer_copy_columns(void* const* dsts, int ndst, const void* sr
         if (e != cudaSuccess) return static_cast<int>(e);
     }
     return 0;
+}
+
+// ---------------------------------------------------------------------------
+// Rotation fused into the producer of x: LayerNorm + modulation, then rotate +
+// quantize, in one pass over x (no reference counterpart: the reference
+// quantizes the activation the model's own LayerNorm/modulation kernels wrote).
+// ---------------------------------------------------------------------------
+
+namespace convrot {
+
+int check_lnmod_args(const void* x, const void* mod_scale, const void* mod_shift, float eps, int M, int K, int G) {
+    if (M < 0 || K <= 0) return fail("M must be >= 0 and K > 0");
+    if (!(G == 64 || G == 256)) return fail("G must be 64 or 256 for the fused LayerNorm form");
+    if (K % 256 != 0 || K > kQ5LnMaxK) return fail("K must be a multiple of 256 and at most 6144");
+    if (!(eps >= 0.0f)) return fail("eps must be >= 0");
+    if (M > 0 && !x) return fail("null activation pointer");
+    if (!aligned16(x) || (reinterpret_cast<uintptr_t>(mod_scale) & 1u) || (reinterpret_cast<uintptr_t>(mod_shift) & 1u))
+        return fail("x must be 16-byte aligned, the modulation vectors 2-byte aligned");
+    return 0;
+}
+
+template <bool UNPACKED>
+int launch_quant_lnmod(const void* x, const LnModArgs& ln, void* q, void* s, int M, int K, int G, cudaStream_t stream) {
+    return G == 256 ? launch_quant_bf16_tiles<256, 4, UNPACKED, true>(x, q, s, M, K, stream, ln)
+                    : launch_quant_bf16_tiles<64, 4, UNPACKED, true>(x, q, s, M, K, stream, ln);
+}
+
+}  // namespace convrot
+
+CONVROT_API int ck_convrot_quant_int4_lnmod(const void* x, const void* mod_scale, const void* mod_shift, float eps,
+                                            void* qout, void* scaleout, int M, int K, int G, int unpacked,
+                                            void* stream) {
+    if (int rc = check_lnmod_args(x, mod_scale, mod_shift, eps, M, K, G)) return rc;
+    if (M == 0) return 0;
+    if (!qout || !scaleout || (reinterpret_cast<uintptr_t>(qout) & 7u)) return fail("qout (8-byte aligned) and scaleout needed");
+    const LnModArgs ln{static_cast<const __nv_bfloat16*>(mod_scale), static_cast<const __nv_bfloat16*>(mod_shift), eps};
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return unpacked ? launch_quant_lnmod<true>(x, ln, qout, scaleout, M, K, G, s)
+                    : launch_quant_lnmod<false>(x, ln, qout, scaleout, M, K, G, s);
+}
+
+CONVROT_API int ck_convrot_w4a4_linear_lnmod(const void* x, const void* mod_scale, const void* mod_shift, float eps,
+                                             const void* Wp, const void* wscale, const void* bias, int bias_dtype,
+                                             void* out, int out_dtype, int M, int N, int K, int G, void* workspace,
+                                             size_t workspace_bytes, void* stream) {
+    if (int rc = check_lnmod_args(x, mod_scale, mod_shift, eps, M, K, G)) return rc;
+    if (int rc = check_linear_args(x, 1, Wp, wscale, bias_dtype, out, out_dtype, M, N, K, G)) return rc;
+    if (M == 0 || N == 0) return 0;
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255u)) return fail("workspace must be 256-byte aligned");
+    if (workspace_bytes < linear_workspace_bytes(M, K))
+        return fail("workspace smaller than ck_convrot_w4a4_linear_workspace_size(M, K)");
+    const LnModArgs ln{static_cast<const __nv_bfloat16*>(mod_scale), static_cast<const __nv_bfloat16*>(mod_shift), eps};
+    const float* ws = static_cast<const float*>(wscale);
+    const BiasRef b{bias, bias_dtype};
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    unsigned char* q = static_cast<unsigned char*>(workspace);
+    if (a8_eligible(1, M, K, G)) {
+        float* xs = reinterpret_cast<float*>(q + ((static_cast<size_t>(M) * K + 255) & ~static_cast<size_t>(255)));
+        if (int rc = launch_quant_lnmod<true>(x, ln, q, xs, M, K, G, s)) return rc;
+        if (out_dtype == 1) return dispatch_gemm_a8<kOutBF16>(q, Wp, xs, ws, b, out, M, N, K, LoraArgs(), s);
+        return dispatch_gemm_a8<kOutF32>(q, Wp, xs, ws, b, out, M, N, K, LoraArgs(), s);
+    }
+    float* xs = reinterpret_cast<float*>(q + ((static_cast<size_t>(M) * (K / 2) + 255) & ~static_cast<size_t>(255)));
+    if (int rc = launch_quant_lnmod<false>(x, ln, q, xs, M, K, G, s)) return rc;
+    if (out_dtype == 1) return dispatch_gemm<kOutBF16>(q, Wp, xs, ws, b, out, M, N, K, s);
+    return dispatch_gemm<kOutF32>(q, Wp, xs, ws, b, out, M, N, K, s);
 }

@@ -172,6 +172,31 @@ int ck_int8_convrot_gemm(const void* X, const void* W, const void* xscale, const
  * parity checks, like ck_int4_gemm_s32). */
 int ck_int8_gemm_s32(const void* X, const void* W, void* acc, int M, int N, int K, void* stream);
 
+/* The rotation fused into the producer of x (no reference counterpart; the
+ * reference quantizes what the model's LayerNorm/modulation kernels wrote):
+ * each bf16 row is normalised and modulated as a Flux block does before its
+ * QKV or MLP-up projection,
+ *   y = bf16(bf16(bf16(1 + mod_scale[k]) * xn) + mod_shift[k]),
+ *   xn = bf16((x - mean) * rstd), rstd = 1 / sqrt(var + eps)
+ * (LayerNorm without affine, biased variance; fp32 statistics in a fixed order:
+ * lane l of a warp sums elements l, l + 32, ... then an xor butterfly of the 32
+ * lane sums), then rotated and quantized exactly as ck_convrot_quant_int4 would
+ * quantize y. y never goes to memory. mod_scale / mod_shift: bf16 [K], one
+ * vector for all M rows (call once per batch item), NULL = zeros (plain
+ * LayerNorm). bf16 x only; G in {64, 256}; K % 256 == 0, K <= 6144.
+ * unpacked = 1 writes one sign-extended int8 per code ([M, K], the A8 form's
+ * operand), 0 packed codes ([M, K/2]). */
+int ck_convrot_quant_int4_lnmod(const void* x, const void* mod_scale, const void* mod_shift, float eps,
+                                void* qout, void* scaleout, int M, int K, int G, int unpacked, void* stream);
+
+/* ck_convrot_w4a4_linear of the modulated LayerNorm of x (as above), one pass
+ * over x: out = y @ W^T + bias with the int4 path's arithmetic; same workspace
+ * size rule (ck_convrot_w4a4_linear_workspace_size). */
+int ck_convrot_w4a4_linear_lnmod(const void* x, const void* mod_scale, const void* mod_shift, float eps,
+                                 const void* Wp, const void* wscale, const void* bias, int bias_dtype,
+                                 void* out, int out_dtype, int M, int N, int K, int G, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
 /* Column-split linear over peer memory (no reference counterpart: the
  * reference runs on one device). P ranks (one process per GPU) each own N/P
  * weight rows; every rank's GEMM stores its column block straight into every

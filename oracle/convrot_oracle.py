@@ -208,6 +208,59 @@ def _quantize_rowwise(xr: np.ndarray, dtype: str, qmax: int) -> tuple[np.ndarray
     return q, scale.reshape(-1).astype(np.float32)
 
 
+def layernorm_modulate(x_bits: np.ndarray, scale_bits=None, shift_bits=None, eps: float = 1e-6) -> np.ndarray:
+    """(1 + scale) * LayerNorm(x) + shift of bf16 rows (storage bits in, bits out).
+
+    The producer of x before a Flux block's QKV and MLP-up projections (LayerNorm
+    without affine, biased variance; per-channel modulation vectors [K]), in the
+    fixed fp32 order of the fused kernel ``ck_convrot_quant_int4_lnmod``: the row
+    is cut into 128-value segments (half a 256-column tile each, in order); a
+    segment's sum is a binary tree over its sixteen 8-value chunks of binary-tree
+    chunk sums; the segment sums are added in order; mean = sum / K; the squared
+    deviations (x - mean)^2 (two roundings) the same way; rstd =
+    1 / sqrt(var + eps), each step rounded; xn = bf16((x - mean) * rstd);
+    y = bf16(bf16(bf16(1 + scale) * xn) + shift). The model code behind it
+    (ComfyUI's Flux blocks) is not part of the reference; this is the fused
+    kernel's own definition, close to torch.nn.functional.layer_norm followed
+    by the bf16 modulation (``tests/test_oracle_lnmod.py``).
+    """
+    f32 = np.float32
+    v = bf16_bits_to_f32(x_bits)
+    m, k = v.shape
+    if k % 256:
+        raise ValueError("K must be a multiple of 256")
+
+    def warp_sum(vals):
+        c = vals.reshape(m, k // 128, 16, 8)
+        while c.shape[-1] > 1:                      # chunk sums: pairs, quads, all 8
+            c = (c[..., 0::2] + c[..., 1::2]).astype(f32)
+        c = c[..., 0]
+        while c.shape[-1] > 1:                      # segment sums over the 16 chunks
+            c = (c[..., 0::2] + c[..., 1::2]).astype(f32)
+        part = c[..., 0]
+        acc = part[:, 0]
+        for i in range(1, part.shape[1]):
+            acc = (acc + part[:, i]).astype(f32)
+        return acc
+
+    with np.errstate(over="ignore", invalid="ignore", divide="ignore"):
+        mean = (warp_sum(v) / f32(k)).astype(f32)
+        d = (v - mean[:, None]).astype(f32)
+        var = (warp_sum((d * d).astype(f32)) / f32(k)).astype(f32)
+        rstd = (f32(1.0) / np.sqrt((var + f32(eps)).astype(f32))).astype(f32)
+        xn = round_to_bf16((d * rstd[:, None]).astype(f32))
+        s1 = np.ones(k, f32) if scale_bits is None else round_to_bf16((f32(1.0) + bf16_bits_to_f32(scale_bits)).astype(f32))
+        sh = np.zeros(k, f32) if shift_bits is None else bf16_bits_to_f32(shift_bits)
+        t2 = round_to_bf16((s1[None, :] * xn).astype(f32))
+        y = round_to_bf16((t2 + sh[None, :]).astype(f32))
+    return f32_to_bf16_bits(y)
+
+
+def convrot_quant_int4_lnmod(x_bits, scale_bits, shift_bits, eps: float, group: int):
+    """Packed codes and scales of the modulated LayerNorm of x (``ck_convrot_quant_int4_lnmod``)."""
+    return convrot_quant_int4(layernorm_modulate(x_bits, scale_bits, shift_bits, eps), group, "bf16")
+
+
 def pack_int4(codes: np.ndarray) -> np.ndarray:
     """[..., K] int4 values -> [..., K/2] int8; even column in the low nibble."""
     codes = np.asarray(codes)

@@ -193,3 +193,26 @@ def test_lora_down_preconditions(lib):
     assert f(256, 0, 256, 256, 16, 256, 8, None) == -1 and b"dtype" in lib.ck_convrot_last_error()
     assert f(264, 1, 256, 256, 16, 256, 8, None) == -1 and b"aligned" in lib.ck_convrot_last_error()
     assert f(256, 1, 256, 256, 0, 256, 8, None) == 0                                             # M = 0: no launch
+
+
+def test_lnmod_preconditions(lib):
+    f = lib.ck_convrot_quant_int4_lnmod
+    assert f(256, 0, 0, 1e-6, 256, 256, 4, 320, 64, 0, None) == -1 and b"256" in lib.ck_convrot_last_error()
+    assert f(256, 0, 0, 1e-6, 256, 256, 4, 8192, 256, 0, None) == -1                 # K > 6144
+    assert f(256, 0, 0, 1e-6, 256, 256, 4, 3072, 16, 0, None) == -1                  # G = 16
+    assert f(264, 0, 0, 1e-6, 256, 256, 4, 3072, 256, 0, None) == -1 and b"aligned" in lib.ck_convrot_last_error()
+    assert f(256, 0, 0, -1.0, 256, 256, 4, 3072, 256, 0, None) == -1                 # eps < 0
+    assert f(256, 0, 0, 1e-6, 256, 256, 0, 3072, 256, 0, None) == 0                  # M = 0: no launch
+
+
+def test_peer_entry_preconditions(lib):
+    outs = (ctypes.c_void_p * 2)(256, 512)
+    f = lib.ck_int4_convrot_gemm_a8_peers
+    assert f(256, 256, 256, 256, 0, 0, outs, 9, 3072, 0, 16, 1536, 3072, 1, 0, 0, 0, ctypes.c_float(0), None) == -1
+    assert f(256, 256, 256, 256, 0, 0, outs, 2, 3000, 1536, 16, 1536, 3072, 1, 0, 0, 0, ctypes.c_float(0), None) == -1
+    assert f(256, 256, 256, 256, 0, 0, outs, 2, 3072, 4, 16, 1536, 3072, 1, 0, 0, 0, ctypes.c_float(0), None) == -1
+    flags = (ctypes.c_void_p * 2)(256, 512)
+    assert lib.ck_peer_barrier(flags, 9, 0, 256, 1000, None) == -1
+    assert lib.ck_peer_barrier(flags, 2, 2, 256, 1000, None) == -1
+    assert lib.ck_peer_barrier(flags, 2, 0, 256, 0, None) == -1
+    assert lib.ck_peer_copy_columns(flags, 1, 256, 64, 32, 64, 4, None) == -1     # offset + width > pitch
