@@ -579,6 +579,7 @@ class FluxDiT:
         self.gen = torch.Generator(device=device).manual_seed(seed)
         self.int4_layers = 0
         self.Q = Int4ConvRotLinear
+        self.fused_ln = True
 
         def lin(name, k, n):
             if k >= 512 and not any(s in name for s in FLUX_SKIP):
@@ -653,6 +654,13 @@ class FluxDiT:
     def _ln_mod(self, x, shift, scale):
         return torch.nn.functional.layer_norm(x, (self.hidden,), eps=1e-6) * (1 + scale) + shift
 
+    def _ln_mod_lin(self, lin, x, shift, scale):
+        """lin((1 + scale) * LayerNorm(x) + shift): int4 layers take the normalisation into their
+        rotate + quantize pass (fused_ln), otherwise torch normalises first."""
+        if self.fused_ln and isinstance(lin, self.Q):
+            return lin.forward_lnmod(x, shift, scale, eps=1e-6)
+        return lin(self._ln_mod(x, shift, scale))
+
     def _heads(self, qkv, qn, kn):
         L = qkv.shape[0]
         q, k, v = qkv.view(L, 3, self.heads, 128).permute(1, 2, 0, 3)
@@ -684,28 +692,28 @@ class FluxDiT:
             qkv = {}
             for s in ("txt", "img"):
                 sh, sc, _, _, _, _ = mods[s]
-                qkv[s] = self._heads(blk[s]["qkv"](self._ln_mod(streams[s], sh, sc)), blk[s]["qn"], blk[s]["kn"])
+                qkv[s] = self._heads(self._ln_mod_lin(blk[s]["qkv"], streams[s], sh, sc), blk[s]["qn"], blk[s]["kn"])
             q, k, v = (torch.cat([qkv["txt"][i], qkv["img"][i]], dim=1) for i in range(3))
             attn = self._attend(q, k, v, cos, sin)
             outs = {"txt": attn[:n_txt], "img": attn[n_txt:]}
             for s in ("txt", "img"):
                 _, _, g1, sh2, sc2, g2 = mods[s]
                 x = streams[s] + g1 * blk[s]["proj"](outs[s])
-                mlp = blk[s]["mlp2"](torch.nn.functional.gelu(blk[s]["mlp0"](self._ln_mod(x, sh2, sc2)),
+                mlp = blk[s]["mlp2"](torch.nn.functional.gelu(self._ln_mod_lin(blk[s]["mlp0"], x, sh2, sc2),
                                                               approximate="tanh"))
                 streams[s] = x + g2 * mlp
             img, txt = streams["img"], streams["txt"]
         x = torch.cat([txt, img], dim=0)
         for blk in self.single:
             sh, sc, g = blk["mod"](svec).chunk(3, dim=-1)
-            lin1 = blk["linear1"](self._ln_mod(x, sh, sc))
+            lin1 = self._ln_mod_lin(blk["linear1"], x, sh, sc)
             q, k, v = self._heads(lin1[:, :3 * h], blk["qn"], blk["kn"])
             attn = self._attend(q, k, v, cos, sin)
             mlp = torch.nn.functional.gelu(lin1[:, 3 * h:], approximate="tanh")
             x = x + g * blk["linear2"](torch.cat([attn, mlp], dim=-1))
         img = x[n_txt:]
         sh, sc = self.final_mod(svec).chunk(2, dim=-1)
-        out = self.final(self._ln_mod(img, sh, sc))
+        out = self._ln_mod_lin(self.final, img, sh, sc)
         return out.view(hh, ww, c, 2, 2).permute(2, 0, 3, 1, 4).reshape(1, c, hh * 2, ww * 2)
 
 
@@ -726,7 +734,17 @@ def dit_step_leg(device, flush, stream, steps):
     replay, graph = graphed(fwd, flush)
     ms = timed_steps(replay, steps, flush, stream, 1, device)
     del graph
-    return {"ms": ms, "int4_linears": model.int4_layers, "tokens": 4096 + 512,
+    # the same step with torch normalising before every int4 projection (no fused producer)
+    model.fused_ln = False
+    for _ in range(2):
+        fwd()
+    replay, graph = graphed(fwd, flush)
+    ms_unfused = timed_steps(replay, steps, flush, stream, 1, device)
+    del graph
+    model.fused_ln = True
+    return {"ms": ms, "unfused_ln_ms": ms_unfused, "int4_linears": model.int4_layers, "tokens": 4096 + 512,
+            "fused_ln": "LayerNorm + modulation before QKV / MLP-up / linear1 inside the int4 quantizer "
+                        "(ck_convrot_w4a4_linear_lnmod); unfused_ln_ms: torch normalises first",
             "inputs": "latent [1,16,128,128], text [1,512,4096] ~ N(0,1), pooled [1,768] ~ N(0,1), t=0.5, "
                       "guidance=3.5 (seeded)",
             "launch": "CUDA graph replay, L2 flushed before each step"}

@@ -16,8 +16,8 @@ from __future__ import annotations
 
 import torch
 
-from . import (checkpoint, convrot_w4a4_linear, convrot_w4a4_linear_lora, convrot_w8a8_linear_lora,
-               pick_groupsize)
+from . import (checkpoint, convrot_w4a4_linear, convrot_w4a4_linear_lnmod, convrot_w4a4_linear_lora,
+               convrot_w8a8_linear_lora, cuda_loader, pick_groupsize)
 from .eager import quantize_convrot_w4a4_weight
 
 _CKPT_KEYS = ("weight", "weight_scale", "comfy_quant", "bias")
@@ -96,6 +96,22 @@ class Int4ConvRotLinear(torch.nn.Module):
             prepared.append((down.to(self._q.device, torch.float16), up.to(self._q.device, torch.float16),
                              float(alpha) / r * float(strength)))
         self._dyn_lora = prepared
+
+    def forward_lnmod(self, x: torch.Tensor, shift: torch.Tensor | None, scale: torch.Tensor | None,
+                      eps: float = 1e-6) -> torch.Tensor:
+        """``self((1 + scale) * layer_norm(x) + shift)``, the input a Flux block feeds its QKV and
+        MLP-up projections. Plain int4 layers on bf16 rows of whole tiles run it in one pass
+        over x (``_int4.convrot_w4a4_linear_lnmod``: the normalised rows never reach memory);
+        int8 layers and layers with Dynamic-LoRA adapters normalise in torch first."""
+        if self._qmode == "int4" and not self._dyn_lora and cuda_loader.lnmod_supported(x, self._qgs):
+            return convrot_w4a4_linear_lnmod(x, self._q, self._qs, self.bias, shift=shift, scale=scale, eps=eps,
+                                             convrot_groupsize=self._qgs)
+        xn = torch.nn.functional.layer_norm(x, (x.shape[-1],), eps=eps)
+        if scale is not None:
+            xn = xn * (1 + scale)
+        if shift is not None:
+            xn = xn + shift
+        return self(xn)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self._qmode == "int8":

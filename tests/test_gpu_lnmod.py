@@ -112,3 +112,29 @@ def test_lnmod_rejects_bad_shapes(ck):
     x = torch.zeros(4, 8192, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(RuntimeError):
         ck.convrot_quant_int4_lnmod(x, None, None, 1e-6, 256, False)     # K > 6144
+
+
+def test_module_forward_lnmod(ck):
+    """Int4ConvRotLinear.forward_lnmod: the fused pass for plain int4 layers; with a
+    Dynamic-LoRA adapter, torch normalises first and the LoRA linear runs."""
+    import _int4
+    from _int4.linear import Int4ConvRotLinear
+    m, k, n = 300, 3072, 1024
+    x, scale, shift = rows(m, k, seed=21)
+    g = torch.Generator().manual_seed(22)
+    lin = Int4ConvRotLinear(k, n, True, device="cuda")
+    qw, ws = _int4.quantize_convrot_w4a4_weight((torch.randn(n, k, generator=g) * 0.02).to(torch.float16).cuda(), 256)
+    lin._q.copy_(qw)
+    lin._qs.copy_(ws)
+    got = lin.forward_lnmod(x, shift, scale)
+    want = _int4.convrot_w4a4_linear_lnmod(x, qw, ws, lin.bias, shift=shift, scale=scale)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    down = (torch.randn(16, k, generator=g) * 0.01).cuda()
+    up = (torch.randn(n, 16, generator=g) * 0.01).cuda()
+    lin.set_dynamic_lora([(down, up, 16.0, 1.0)])
+    got = lin.forward_lnmod(x, shift, scale)
+    xn = torch.nn.functional.layer_norm(x, (k,), eps=1e-6) * (1 + scale) + shift
+    want = lin(xn)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
