@@ -986,6 +986,8 @@ def run_case(args):
     gen = torch.Generator().manual_seed(0)
     if args.case == "small_m":
         m, k, n = 1, 3072, 18432
+    elif args.case == "lora_down":
+        m, k, n = M_TOKENS, 12288, 3072          # config 4's MLP-down input, rank 64
     else:
         m, k, n = M_TOKENS, 3072, 12288
     if args.m:
@@ -1002,8 +1004,15 @@ def run_case(args):
     else:
         xq, xsc = ck.convrot_quant_int4(x, GROUP)
     flush_buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+    down = (torch.randn(64, k, generator=gen) * 0.01).to(torch.float16).to(device)
+    mod_scale = (torch.randn(k, generator=gen) * 0.2).to(torch.bfloat16).to(device)
+    mod_shift = (torch.randn(k, generator=gen) * 0.2).to(torch.bfloat16).to(device)
     for _ in range(args.iters):
-        if args.case == "quant":
+        if args.case == "lora_down":
+            ck.lora_down(x, down)
+        elif args.case == "lnmod_quant":
+            ck.convrot_quant_int4_lnmod(x, mod_scale, mod_shift, 1e-6, GROUP, True)
+        elif args.case == "quant":
             ck.convrot_quant_int4(x, GROUP)
         elif args.case == "quant_unpacked":
             ck.convrot_quant_int4_unpacked(x, GROUP)
@@ -1031,7 +1040,8 @@ def main():
                     help="only the main step (no probes, replicas, N-split or DiT legs)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="launch every kernel from the host each step instead of replaying a CUDA graph")
-    ap.add_argument("--case", choices=["mlp_up", "small_m", "quant", "mlp_up_unpacked", "quant_unpacked", "mlp_up_a8"],
+    ap.add_argument("--case", choices=["mlp_up", "small_m", "quant", "mlp_up_unpacked", "quant_unpacked", "mlp_up_a8",
+                                       "lora_down", "lnmod_quant"],
                     default=None,
                     help="run one kernel --iters times (profiling helper) instead of the benchmark")
     ap.add_argument("--iters", type=int, default=3)

@@ -1745,15 +1745,29 @@ int launch_lora_down(const void* x, const void* down, void* t, int M, int K, int
         if (ksplit < 1) ksplit = 1;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(m_tiles) * static_cast<unsigned>(ksplit), 1, 1);
     cfg.blockDim = dim3(kLdThreads, 1, 1);
     cfg.dynamicSmemBytes = kLdSmemBytes;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = static_cast<unsigned>(ksplit);
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // clusters of ksplit CTAs only fit where a GPC has ksplit free SMs: split less
+    // until every tile's cluster is resident at once (a second wave doubles the time)
+    for (; ksplit > 1; --ksplit) {
+        attr[0].val.clusterDim.x = static_cast<unsigned>(ksplit);
+        cfg.gridDim = dim3(static_cast<unsigned>(m_tiles) * static_cast<unsigned>(ksplit), 1, 1);
+        int active = 0;
+        if (cudaOccupancyMaxActiveClusters(&active, kernel, &cfg) != cudaSuccess) {
+            (void)cudaGetLastError();
+            continue;
+        }
+        if (active >= m_tiles) break;
+    }
+    attr[0].val.clusterDim.x = static_cast<unsigned>(ksplit);
+    cfg.gridDim = dim3(static_cast<unsigned>(m_tiles) * static_cast<unsigned>(ksplit), 1, 1);
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
