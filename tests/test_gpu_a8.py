@@ -139,3 +139,25 @@ def test_fused_linear_a8_vs_oracle(ck, m, k, n, g):
     assert np.array_equal(bits(out)[rows], ref)
     assert ck.device_status() == 0
 
+
+
+@pytest.mark.parametrize("m", [5, 17, 64, 65, 100, 128])
+@pytest.mark.parametrize("k,n", [(3072, 18432), (12288, 3072), (256, 264)])
+def test_public_linear_small_m_a8t_vs_oracle(m, k, n):
+    """The public linear at 5 to 128 bf16 rows (swapped-tile GEMMs on packed codes) against
+    the oracle at config-sized layers and a ragged one: bf16 bits equal."""
+    import _int4
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    g = torch.Generator().manual_seed(m * 31 + k + n)
+    x = torch.randn(m, k, generator=g)
+    x[:, torch.randperm(k, generator=g)[: max(1, k // 100)]] *= 20
+    x = x.to(torch.bfloat16).cuda()
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.float16).cuda()
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.float16).cuda()
+    qw, ws = _int4.quantize_convrot_w4a4_weight(w, 256)
+    out = _int4.convrot_w4a4_linear(x, qw, ws, bias=bias, convrot_groupsize=256)
+    torch.cuda.synchronize()
+    xb = x.cpu().view(torch.int16).numpy().view(np.uint16)
+    ref = orc.convrot_w4a4_linear(xb, qw.cpu().numpy(), ws.cpu().numpy(), bias.float().cpu().numpy(), 256)
+    assert np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), ref)
