@@ -775,7 +775,13 @@ def nsplit_leg(device, rank, world, flush, stream, steps):
     adapters = shard_adapters(down["adapters"], rank, world)
     gather = lambda: convrot_w4a4_linear_lora_nsplit(x, q, w, b, adapters, GROUP)
     res = {}
-    split = PeerColumnSplit(device=device) if peer_split_supported(x, q.shape[0], GROUP) else None
+    from _int4.nsplit import PeerSplitUnavailable
+    split = None
+    if peer_split_supported(x, q.shape[0], GROUP):
+        try:
+            split = PeerColumnSplit(device=device)
+        except PeerSplitUnavailable:     # every rank sees the same outcome
+            split = None
     legs = [("nccl_all_gather", gather)]
     if split is not None:
         legs.insert(0, ("peer_stores", lambda: convrot_w4a4_linear_peer_split(x, q, w, b, adapters, split, GROUP)))

@@ -138,6 +138,10 @@ class _HostArrayView:
 _VIEW_TYPES = {torch.bfloat16: ("<i2", torch.int16), torch.float32: ("<f4", torch.float32)}
 
 
+class PeerSplitUnavailable(RuntimeError):
+    """Raised on every rank when some rank cannot map a peer's buffer."""
+
+
 class PeerColumnSplit:
     """Peer-memory resources of the column-split linear for one process group.
 
@@ -163,7 +167,11 @@ class PeerColumnSplit:
         self._own: list[int] = []
         self._opened: list[int] = []
         flags = self._alloc(256)
-        self.flag_ptrs = self._exchange(flags)
+        try:
+            self.flag_ptrs = self._exchange(flags)
+        except PeerSplitUnavailable:
+            self.close()                 # every rank is on this path: the barriers in close() match
+            raise
         self.counter = flags[0] + 128
         self._outs: dict = {}
         self.copy_stream = torch.cuda.Stream(self.device)
@@ -175,18 +183,29 @@ class PeerColumnSplit:
         return ptr, handle
 
     def _exchange(self, own) -> list[int]:
-        """Every rank's pointer to its buffer (this rank's own, the others' opened)."""
+        """Every rank's pointer to its buffer (this rank's own, the others' opened). The
+        ranks agree on the outcome: if any rank fails to map a peer's buffer, every
+        rank raises PeerSplitUnavailable (so none is left waiting in a collective)."""
         handles = [None] * self.world
         dist.all_gather_object(handles, own[1], group=self.group)
         ptrs = []
+        err = None
         with torch.cuda.device(self.device):
             for p, h in enumerate(handles):
                 if p == self.rank:
                     ptrs.append(own[0])
-                else:
+                    continue
+                try:
                     q = cuda_loader.peer_buffer_open(h)
-                    self._opened.append(q)
-                    ptrs.append(q)
+                except RuntimeError as e:          # no peer mapping between these devices
+                    err = e
+                    break
+                self._opened.append(q)
+                ptrs.append(q)
+        ok = torch.tensor([0 if err else 1], dtype=torch.int32, device=self.device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
+        if int(ok.item()) == 0:
+            raise PeerSplitUnavailable(f"a rank could not map a peer's buffer ({err or 'on another rank'})")
         return ptrs
 
     def output(self, m: int, n: int, dtype: torch.dtype):
