@@ -844,6 +844,16 @@ def run_ours(args, rank, world, local_rank):
     value = ops_total / (ms_per_step * 1e-3) / 1e12
     del graph
 
+    # ---------------- each layer of the step on its own (graph, L2 flushed, max over ranks):
+    # which layer limits the step at this N
+    layers_ms = {}
+    if args.extras and args.graph:
+        for l in layers:
+            fn, g = graphed(lambda l=l: run_layer(l, xs[l["key"]]), flush)
+            layers_ms[f"{l['name']} M={l['m']} {l['k']}->{l['n']}"] = timed_steps(fn, min(args.steps, 20), flush,
+                                                                                 stream, world, device)
+            del g
+
     # ---------------- end to end: host buffers in, host buffers out, through the public API
     e2e = e2e_leg(layers, xs, device, stream, world, args.steps)
     e2e_value = ops_total / (e2e["ms_per_step"] * 1e-3) / 1e12
@@ -901,6 +911,7 @@ def run_ours(args, rank, world, local_rank):
             "config": workload_config(cfg_id, world if split else 1,
                                       {"launch": "CUDA graph replay" if args.graph else "eager launches"}),
             "gpu_launches": 2 * len(layers) * args.steps,
+            **({"layers_ms": layers_ms} if layers_ms else {}),
             "clocks": clocks,
             "e2e": {"value": e2e_value, "unit": UNIT, **e2e},
             **extras,
