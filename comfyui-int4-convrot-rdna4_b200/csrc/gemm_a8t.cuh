@@ -155,6 +155,16 @@ int4_gemm_a8t_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_co
     tc_fence_before();
     cluster_sync();                       // peer barriers initialised before any remote arrive
     tc_fence_after();
+    if (warp == 3 && lane == 0 && cluster_id < num_tiles) {
+        // an L2 hint, safe whatever the previous kernel writes: this CTA's weight rows of
+        // its first tile (one contiguous block of packed bytes) start streaming while the
+        // previous kernel (the quantizer) still runs
+        const int w_row0 = (cluster_id % tiles_w) * 256 + static_cast<int>(cta) * Cfg::kWRows;
+        const int rows = N - w_row0 < Cfg::kWRows ? N - w_row0 : Cfg::kWRows;
+        if (rows > 0)
+            bulk_prefetch_l2(static_cast<const unsigned char*>(wraw) + static_cast<size_t>(w_row0) * (K >> 1),
+                             static_cast<uint32_t>(rows) * static_cast<uint32_t>(K >> 1));
+    }
     // every operand, scale and output may belong to the previous kernel
     griddep_wait();
     griddep_launch_dependents();
@@ -243,14 +253,7 @@ int4_gemm_a8t_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_co
             }
         }
     } else if (warp == 3) {
-        if (lane == 0 && cluster_id < num_tiles) {
-            // this CTA's weight rows of its first tile are one contiguous block of packed bytes
-            const int w_row0 = (cluster_id % tiles_w) * 256 + static_cast<int>(cta) * Cfg::kWRows;
-            const int rows = N - w_row0 < Cfg::kWRows ? N - w_row0 : Cfg::kWRows;
-            if (rows > 0)
-                bulk_prefetch_l2(static_cast<const unsigned char*>(wraw) + static_cast<size_t>(w_row0) * (K >> 1),
-                                 static_cast<uint32_t>(rows) * static_cast<uint32_t>(K >> 1));
-        }
+        // (its L2 prefetch ran before the wait for the previous kernel)
     } else if (warp < 12) {
         // ---------------- expanders: weight row r of the slot -> TMEM lane r
         const int group = (warp - 4) / Cfg::kGroupWarps;
