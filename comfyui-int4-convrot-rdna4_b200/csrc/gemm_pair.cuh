@@ -314,13 +314,15 @@ int4_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
     tc_fence_before();
     cluster_sync();                       // peer barriers initialised before any remote arrive
     tc_fence_after();
+    // int8 and A8 forms: warp 3 has no role, so it pulls the weight boxes of this CTA's
+    // first tile into L2 ahead of the ring, after the sync (one prefetch per
+    // k-stage; issued before the sync they held every warp back). The A8 form's
+    // single contiguous prefetch goes before the wait for the previous kernel.
+    if (A8 && warp == 3 && lane == 0) prefetch_first_weights();
     // every operand, scale and output may belong to the previous kernel
     griddep_wait();
     griddep_launch_dependents();
-    // int8 and A8 forms: warp 3 has no role, so it pulls the weight boxes of this CTA's
-    // first tile into L2 ahead of the ring, after the sync (one prefetch per
-    // k-stage; issued before the sync they held every warp back).
-    if (Cfg::kASmem && warp == 3 && lane == 0) prefetch_first_weights();
+    if (Cfg::kASmem && !A8 && warp == 3 && lane == 0) prefetch_first_weights();
     const uint32_t tmem_base = *tmem_slot;
     const uint32_t tmem_a0 = tmem_base + Cfg::kAccCols * Cfg::kAccBufs;  // A stages follow the accumulators
     // fp32 LoRA accumulator (LORA only): the second half of each accumulator buffer
