@@ -260,7 +260,8 @@ int ck_lora_down(const void* x, int in_dtype, const void* down, void* t, int M, 
  *   (scales and bias ignored); K % 128 == 0, K <= 65536.
  * Optional Dynamic-LoRA side path as ck_int4_convrot_gemm_lora (lora_t, lora_b
  * fp16 [M, rank] / [N, rank], rank a multiple of 8 in [8, 64]; both NULL: none).
- * The weights stay packed in HBM and are expanded in shared memory; the
+ * The weights stay packed in HBM and are expanded on chip (into tensor memory
+ * for grids of 74+ output tiles without LoRA, else in shared memory); the
  * activations go to the tensor cores as loaded. Same D, epilogue and output
  * bits as the packed-code GEMM. */
 int ck_int4_convrot_gemm_a8(const void* X8, const void* Wp, const void* xscale, const void* wscale,
