@@ -1558,9 +1558,18 @@ int dispatch_gemm_a8(const void* X8, const void* Wp, const float* xs, const floa
     }
     if (CONVROT_A8T_BN > 0) {
         const long tiles_t = static_cast<long>((N + 255) / 256) * ((M + CONVROT_A8T_BN - 1) / CONVROT_A8T_BN);
-        if (2 * tiles_t >= sm_count())
+        if (2 * tiles_t >= sm_count()) {
+            // wave quantization: the share of CTA-pair slots the tiles fill; 192-token
+            // tiles when they fill the last wave much better (e.g. 2304 x 3072: 108
+            // tiles of 256 for 74 pairs fill 73 %, 144 tiles of 192 fill 97 %)
+            const long pairs = sm_count() / 2;
+            const long tiles_192 = static_cast<long>((N + 255) / 256) * ((M + 191) / 192);
+            auto fill = [&](long t) { return static_cast<double>(t) / static_cast<double>(((t + pairs - 1) / pairs) * pairs); };
+            if (CONVROT_A8T_BN == 256 && fill(tiles_192) >= fill(tiles_t) + 0.15)
+                return launch_a8t<192, OUT>(X8, Wp, xs, ws, bias, out, M, N, K, stream);
             return launch_a8t<(CONVROT_A8T_BN > 0 ? CONVROT_A8T_BN : 192), OUT>(X8, Wp, xs, ws, bias, out, M, N, K,
                                                                                stream);
+        }
     }
     if (2 * tiles256 >= sm_count() / 2)
         return launch_pair_impl<256, false, OUT, false, false, false, true>(X8, Wp, xs, ws, bias, out, M, N, K,

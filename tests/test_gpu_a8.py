@@ -161,3 +161,25 @@ def test_public_linear_small_m_a8t_vs_oracle(m, k, n):
     xb = x.cpu().view(torch.int16).numpy().view(np.uint16)
     ref = orc.convrot_w4a4_linear(xb, qw.cpu().numpy(), ws.cpu().numpy(), bias.float().cpu().numpy(), 256)
     assert np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), ref)
+
+
+@pytest.mark.parametrize("m,k,n", [(2304, 12288, 3072), (2304, 3072, 3072), (2200, 3072, 3072)])
+def test_public_linear_192_token_tiles_vs_oracle(m, k, n):
+    """Layers whose 256-token A8T grid leaves the last wave mostly empty take 192-token
+    tiles (a token split of config 1 over two GPUs): sampled rows bit-exact."""
+    import _int4
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    g = torch.Generator().manual_seed(m + k + n)
+    x = torch.randn(m, k, generator=g)
+    x[:, torch.randperm(k, generator=g)[: k // 100]] *= 20
+    x = x.to(torch.bfloat16).cuda()
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.float16).cuda()
+    bias = (torch.randn(n, generator=g) * 0.01).to(torch.float16).cuda()
+    qw, ws = _int4.quantize_convrot_w4a4_weight(w, 256)
+    out = _int4.convrot_w4a4_linear(x, qw, ws, bias=bias, convrot_groupsize=256)
+    torch.cuda.synchronize()
+    rows = np.unique(np.r_[np.random.default_rng(m).choice(m, 48, replace=False), 0, m - 1])
+    xb = x.cpu().view(torch.int16).numpy().view(np.uint16)[rows]
+    ref = orc.convrot_w4a4_linear(xb, qw.cpu().numpy(), ws.cpu().numpy(), bias.float().cpu().numpy(), 256)
+    assert np.array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16)[rows], ref)
