@@ -204,6 +204,10 @@ def _quantize_rowwise(xr: np.ndarray, dtype: str, qmax: int) -> tuple[np.ndarray
     with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
         scale = round_to_dtype(absmax / np.float32(qmax), dtype)
         t = round_to_dtype(v / scale, dtype)
+    # An all-zero fp16 row has scale 0 (the 1e-10 floor underflows in fp16), so its
+    # values are 0/0 = NaN; the reference's NaN -> int8 cast gives code 0 there
+    # (row 3 of the golden case q_g256_f16 in tests/golden/int8.npz).
+    t = np.where(np.isnan(t), np.float32(0), t)
     q = np.clip(np.rint(t), -qmax, qmax).astype(np.int8)
     return q, scale.reshape(-1).astype(np.float32)
 
