@@ -25,10 +25,10 @@ epilogue, and with it the MMAs, 540 against 291 us on 2 GPUs.)
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
-
-import os
 
 from . import _lora_operands, convrot_w4a4_linear, convrot_w4a4_linear_lora, cuda_loader
 
