@@ -25,6 +25,7 @@ epilogue, and with it the MMAs, 540 against 291 us on 2 GPUs.)
 """
 from __future__ import annotations
 
+import contextlib
 import os
 
 import torch
@@ -142,6 +143,18 @@ class PeerSplitUnavailable(RuntimeError):
     """Raised on every rank when some rank cannot map a peer's buffer."""
 
 
+def _all_ranks_ok(ok: bool, group, device) -> bool:
+    """True on every rank exactly when ``ok`` holds on every rank of ``group`` (MIN all-reduce)."""
+    flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+    return bool(int(flag.item()))
+
+
+def _on_device(device: torch.device):
+    """The CUDA device context for ``device`` (none needed for a CPU device)."""
+    return torch.cuda.device(device) if device.type == "cuda" else contextlib.nullcontext()
+
+
 class PeerColumnSplit:
     """Peer-memory resources of the column-split linear for one process group.
 
@@ -177,7 +190,7 @@ class PeerColumnSplit:
         self.copy_stream = torch.cuda.Stream(self.device)
 
     def _alloc(self, nbytes: int):
-        with torch.cuda.device(self.device):
+        with _on_device(self.device):
             ptr, handle = cuda_loader.peer_buffer_alloc(nbytes)
         self._own.append(ptr)
         return ptr, handle
@@ -190,7 +203,7 @@ class PeerColumnSplit:
         dist.all_gather_object(handles, own[1], group=self.group)
         ptrs = []
         err = None
-        with torch.cuda.device(self.device):
+        with _on_device(self.device):
             for p, h in enumerate(handles):
                 if p == self.rank:
                     ptrs.append(own[0])
@@ -202,9 +215,7 @@ class PeerColumnSplit:
                     break
                 self._opened.append(q)
                 ptrs.append(q)
-        ok = torch.tensor([0 if err else 1], dtype=torch.int32, device=self.device)
-        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
-        if int(ok.item()) == 0:
+        if not _all_ranks_ok(err is None, self.group, self.device):
             raise PeerSplitUnavailable(f"a rank could not map a peer's buffer ({err or 'on another rank'})")
         return ptrs
 
@@ -227,9 +238,10 @@ class PeerColumnSplit:
 
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's (collective: every rank calls it)."""
-        torch.cuda.synchronize(self.device)
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
-        with torch.cuda.device(self.device):
+        with _on_device(self.device):
             for q in self._opened:
                 cuda_loader.peer_buffer_close(q)
             dist.barrier(group=self.group)
