@@ -1069,6 +1069,8 @@ def main():
         return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.impl == "reference" and args.config != 1:
+        ap.error("the reference arm times config 1 (the metric's config) only")
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -34,3 +34,18 @@ def test_bench_refuses_short_warmup():
     proc = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "1"],
                           cwd=ROOT, capture_output=True, text=True, timeout=300)
     assert proc.returncode != 0 and "--warmup must be >= 3" in proc.stderr
+
+
+def test_reference_arm_other_ranks_do_no_work():
+    """Under torchrun only rank 0 times the reference; the others exit 0 silently."""
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", RANK="1", WORLD_SIZE="2", LOCAL_RANK="1")
+    proc = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--gpus", "2", "--steps", "1",
+                           "--warmup", "3"], cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    assert not [ln for ln in proc.stdout.splitlines() if ln.startswith("{")]
+
+
+def test_reference_arm_refuses_other_configs():
+    proc = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--config", "4", "--steps", "1",
+                           "--warmup", "3"], cwd=ROOT, capture_output=True, text=True, timeout=300)
+    assert proc.returncode != 0 and "config 1" in proc.stderr
